@@ -1,0 +1,718 @@
+// Kernel C: fused-dequant split-KV decode attention over the compact pool,
+// the cross-shard (o, lse) merge, and the dense selected_attention API.
+//
+// Replaces KVQuantCompactImpl.forward's unpack_to_staging + FlashAttention
+// (xFuzzitx/helix-lite src/kvquant/compact_backend.py:233-299, kernels
+// compact_pool.py:293-395): the selected pages are dequantised on chip and
+// never touch HBM as fp16. Attention math follows
+// src/quest/reference.py:136-168 (softmax(q.K^T * scale) V, fp32 softmax),
+// generalised to grouped-query heads (query head h*G+g reads KV head h).
+//
+// One CTA = (split, KV head, sequence), 4 warps. Each warp streams its pages:
+//   bulk TMA (cp.async.bulk, no multicast) of the page's code segment and its
+//   outlier entries into a 2-stage buffer, LUT dequant of the 16 x 128 K tile
+//   into swizzled smem, outlier patch, ldmatrix + mma.sync (tokens x heads),
+//   online softmax in fp32 (exp2 domain), P split into fp16 hi + lo parts so
+//   P.V keeps ~22 bits, V tile the same way, PV with two MMAs per m-tile.
+// Warps merge in smem; the last CTA of each (b, h) merges the splits.
+#include "common.cuh"
+
+namespace hx {
+
+constexpr int DD = 128;        // head_size
+constexpr int DS = 16;         // page size (tokens)
+constexpr int NW = 4;          // warps per CTA
+constexpr int LISTCAP = 512;   // pages gathered per round
+constexpr int ENTCAP = 128;    // outlier entries staged per page per K|V
+constexpr int SEGMAX = DS * DD;  // codes bytes per page segment at 4+4 bits
+constexpr int PSZ = 8 * DD + 16;  // floats per split partial: O[8][128], m[8], l[8]
+
+struct DecodeParams {
+  hx_pool_layer pool;
+  hx_layer_scales sc;
+  const uint16_t* q;
+  int B, G;
+  float scale_log2;
+  const int32_t* bt;
+  int bt_stride;
+  const int32_t* seq_lens;
+  int page_begin, max_pages, sel_mode;
+  const float* scores;
+  const uint64_t* thresh;
+  int sinks_req;
+  const int32_t* lists;
+  int list_stride;
+  const int32_t* list_counts;
+  int n_splits;
+  float* part;
+  uint32_t* ctr;
+  float* o;
+  float* lse;
+  uint16_t* out16;
+  uint32_t* err;
+};
+
+struct __align__(128) WarpSmem {
+  uint8_t raw[2][SEGMAX];            // code segments, 2 stages
+  uint32_t ent[2][2][ENTCAP];        // [stage][K|V] outlier entries
+  uint16_t tile[DS * DD];            // dequantised K, then V (swizzled rows)
+  uint16_t vlut[DS * 16];            // per-token V levels of the current page
+  uint64_t bar[2];
+};
+
+struct __align__(128) CtaSmem {
+  WarpSmem w[NW];
+  uint16_t klut[16 * DD + 64];       // per-channel K levels (bank-spread)
+  uint16_t vtail[16];                // V levels at positions >= t_cal
+  int32_t pages[LISTCAP];
+  int32_t phys[LISTCAP];
+  int32_t count;
+  int32_t wcount[NW];
+  int32_t last;
+};
+
+// element offset of (token t, channel d) in a swizzled tile: 16-byte chunks
+// of a row are XOR-permuted by t & 7 so ldmatrix rows hit distinct banks
+HX_DEVINL int tile_off(int t, int d) { return t * DD + ((((d >> 3) ^ (t & 7))) << 3) + (d & 7); }
+
+template <int BK, int BV>
+__global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  CtaSmem& sm = *reinterpret_cast<CtaSmem*>(smem_raw);
+  constexpr int NLK = 1 << BK, NLV = 1 << BV;
+  constexpr int RBK = DD * BK / 8, RBV = DD * BV / 8;
+  constexpr int SEG = DS * (RBK + RBV);
+
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int H = p.pool.num_kv_heads;
+  const int bh = b * H + h;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.G;
+  const int Tc = p.sc.t_cal;
+  const int NB = p.pool.num_blocks;
+  const int seq_len = p.seq_lens[b];
+  const int n = min((seq_len + DS - 1) / DS, p.max_pages);
+
+  // ---- per-CTA tables
+  for (int i = tid; i < NLK * DD; i += blockDim.x) {
+    int d = i / NLK, c = i % NLK;
+    sm.klut[NLK * d + 32 * (d >> 6) + c] =
+        c < p.sc.levels_k ? p.sc.k_poles[((int64_t)h * DD + d) * p.sc.levels_k + c] : (uint16_t)0;
+  }
+  if (tid < NLV)
+    sm.vtail[tid] = tid < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + (Tc - 1)) * p.sc.levels_v + tid] : (uint16_t)0;
+  WarpSmem& ws = sm.w[warp];
+  if (lane == 0) {
+    mbar_init(&ws.bar[0], 1);
+    mbar_init(&ws.bar[1], 1);
+    fence_mbar_init();
+  }
+
+  // query fragments (B operand, k = channel, n = head column)
+  const int g = lane >> 2, qd = lane & 3;
+  uint32_t bq[8][2];
+  {
+    const int64_t qrow = ((int64_t)b * H * G + (int64_t)h * G + g) * DD;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      if (g < G) {
+        bq[ks][0] = *reinterpret_cast<const uint32_t*>(p.q + qrow + 16 * ks + 2 * qd);
+        bq[ks][1] = *reinterpret_cast<const uint32_t*>(p.q + qrow + 16 * ks + 2 * qd + 8);
+      } else {
+        bq[ks][0] = 0u;
+        bq[ks][1] = 0u;
+      }
+    }
+  }
+
+  float oacc[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  uint32_t phase = 0;     // bit s = parity to wait for on stage s
+  uint32_t inflight = 0;  // bit s = a bulk copy into stage s not yet waited for
+  bool timed_out = false;
+
+  // ---- split range
+  int total;
+  if (p.sel_mode == HX_SEL_LIST) total = min(p.list_counts[bh], p.list_stride);
+  else total = n;
+  const int per = (total + p.n_splits - 1) / p.n_splits;
+  const int ra = min(split * per, total), re = min(ra + per, total);
+  const int sinks = min(max(p.sinks_req, 0), n);
+  const uint64_t T = p.sel_mode == HX_SEL_THRESHOLD ? p.thresh[bh] : 0ull;
+  const float* sc_bh = p.scores ? p.scores + (int64_t)bh * p.max_pages : nullptr;
+  __syncthreads();
+
+  for (int rb = ra; rb < re; rb += LISTCAP) {
+    const int rend = min(rb + LISTCAP, re);
+    if (tid == 0) sm.count = 0;
+    __syncthreads();
+    // gather the round's selected pages in ascending order
+    for (int base = rb; base < rend; base += blockDim.x) {
+      int idx = base + tid;
+      int j = -1;
+      bool sel = false;
+      if (idx < rend) {
+        j = p.sel_mode == HX_SEL_LIST ? p.lists[(int64_t)bh * p.list_stride + idx] : idx;
+        if (j < 0 || j >= n) {
+          if (p.sel_mode == HX_SEL_LIST) set_err(p.err, HX_DEV_ERR_BOUNDS);
+        } else if (p.sel_mode == HX_SEL_THRESHOLD) {
+          sel = (j < sinks) || order_key64(sc_bh[j], (uint32_t)j) >= T;
+        } else {
+          sel = true;
+        }
+      }
+      int32_t pp = 0;
+      if (sel) {
+        pp = p.bt ? p.bt[(int64_t)b * p.bt_stride + j] : j;
+        if (pp < 0 || pp >= NB) {
+          set_err(p.err, HX_DEV_ERR_BOUNDS);
+          sel = false;
+        }
+      }
+      uint32_t m = __ballot_sync(0xffffffffu, sel);
+      if (lane == 0) sm.wcount[warp] = __popc(m);
+      __syncthreads();
+      int off = sm.count;
+      for (int w = 0; w < warp; ++w) off += sm.wcount[w];
+      if (sel) {
+        int pos = off + __popc(m & ((1u << lane) - 1));
+        sm.pages[pos] = j;
+        sm.phys[pos] = pp;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int c = sm.count;
+        for (int w = 0; w < NW; ++w) c += sm.wcount[w];
+        sm.count = c;
+      }
+      __syncthreads();
+    }
+    const int cnt = sm.count;
+    const int my_n = cnt > warp ? (cnt - warp + NW - 1) / NW : 0;
+
+    // ---- warp pipeline over pages warp, warp + NW, ...
+    auto dir_word = [&](int k) -> uint32_t {
+      // lanes 0-7 read the K and V directory records of the k-th page
+      if (lane < 8) {
+        int pp = sm.phys[warp + NW * k];
+        return p.pool.dir[((int64_t)h * NB + pp) * 8 + lane];
+      }
+      return 0u;
+    };
+    auto issue = [&](int k, uint32_t dw) {
+      if (timed_out) return;
+      inflight |= 1u << (k & 1);
+      const uint32_t offk = __shfl_sync(0xffffffffu, dw, 0), cntk = __shfl_sync(0xffffffffu, dw, 2);
+      const uint32_t offv = __shfl_sync(0xffffffffu, dw, 4), cntv = __shfl_sync(0xffffffffu, dw, 6);
+      if (lane == 0) {
+        const int st = k & 1;
+        const int pp = sm.phys[warp + NW * k];
+        const uint32_t ek = min((cntk + 3u) & ~3u, (uint32_t)ENTCAP);
+        const uint32_t ev = min((cntv + 3u) & ~3u, (uint32_t)ENTCAP);
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&ws.bar[st], SEG + 4u * (ek + ev));
+        bulk_g2s(ws.raw[st], p.pool.codes + ((int64_t)h * NB + pp) * SEG, SEG, &ws.bar[st]);
+        if (ek) bulk_g2s(ws.ent[st][0], p.pool.arena + offk, 4u * ek, &ws.bar[st]);
+        if (ev) bulk_g2s(ws.ent[st][1], p.pool.arena + offv, 4u * ev, &ws.bar[st]);
+      }
+    };
+
+    uint32_t dcur = 0, dn1 = 0;
+    if (my_n > 0) dcur = dir_word(0);
+    if (my_n > 1) dn1 = dir_word(1);
+    if (my_n > 0) issue(0, dcur);
+
+    for (int k = 0; k < my_n; ++k) {
+      const int st = k & 1;
+      if (k + 1 < my_n) issue(k + 1, dn1);
+      uint32_t dn2 = (k + 2 < my_n) ? dir_word(k + 2) : 0u;
+      if (!timed_out) {
+        if (mbar_wait(&ws.bar[st], (phase >> st) & 1u)) {
+          phase ^= 1u << st;
+          inflight &= ~(1u << st);
+        } else {
+          timed_out = true;
+          if (lane == 0) set_err(p.err, HX_DEV_ERR_TIMEOUT);
+        }
+      }
+      if (timed_out) {
+        dcur = dn1;
+        dn1 = dn2;
+        continue;
+      }
+      const uint32_t offk = __shfl_sync(0xffffffffu, dcur, 0), cntk = __shfl_sync(0xffffffffu, dcur, 2);
+      const uint32_t offv = __shfl_sync(0xffffffffu, dcur, 4), cntv = __shfl_sync(0xffffffffu, dcur, 6);
+      const int j = sm.pages[warp + NW * k];
+      const int pos0 = (p.page_begin + j) * DS;
+      const int valid = seq_len - j * DS;  // tokens of this page inside the sequence
+
+      const int t = lane & 15, half = lane >> 4;
+      // ---- K tile: per-channel LUT
+      {
+        const uint8_t* rowp = ws.raw[st] + t * RBK + half * (RBK / 2);
+        const uint16_t* kl = sm.klut + half * (64 * NLK + 32);
+        if (BK == 4) {
+          uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
+          uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+          for (int w8 = 0; w8 < 8; ++w8) {
+            uint16_t v[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) v[jj] = kl[16 * (8 * w8 + jj) + ((wv[w8] >> (4 * jj)) & 15u)];
+            uint4 o4 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
+                                  pack_u16x2(v[6], v[7]));
+            const int chunk = (8 * half + w8) ^ (t & 7);
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
+          }
+        } else {
+          uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              uint16_t v[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj)
+                v[jj] = kl[4 * (16 * w4 + 8 * hh + jj) + ((wv[w4] >> (2 * (8 * hh + jj))) & 3u)];
+              uint4 o4 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
+                                    pack_u16x2(v[6], v[7]));
+              const int chunk = (8 * half + 2 * w4 + hh) ^ (t & 7);
+              *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      for (uint32_t e = lane; e < cntk; e += 32) {
+        uint32_t en = e < ENTCAP ? ws.ent[st][0][e] : p.pool.arena[offk + e];
+        int et = (en >> 24) & 31, ed = (en >> 16) & 255;
+        if (et < DS && ed < DD) ws.tile[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
+        else set_err(p.err, HX_DEV_ERR_BOUNDS);
+      }
+      __syncwarp();
+
+      // ---- S^T = K . Q^T  (16 tokens x 8 head columns)
+      float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a[4];
+        const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int chunk = (2 * ks + (lane >> 4)) ^ (r & 7);
+        ldmatrix_x4(a, ws.tile + r * DD + chunk * 8);
+        mma_16816(sacc, a, bq[ks][0], bq[ks][1]);
+      }
+      // ---- online softmax (exp2 domain); rows = tokens g, g+8; cols = 2qd, 2qd+1
+      float x0 = sacc[0] * p.scale_log2, x1 = sacc[1] * p.scale_log2;
+      float x2 = sacc[2] * p.scale_log2, x3 = sacc[3] * p.scale_log2;
+      if (g >= valid) x0 = x1 = -INFINITY;
+      if (g + 8 >= valid) x2 = x3 = -INFINITY;
+      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+      for (int s = 4; s <= 16; s <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, s));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, s));
+      }
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float bs0 = mn0 == -INFINITY ? 0.0f : mn0, bs1 = mn1 == -INFINITY ? 0.0f : mn1;
+      const float al0 = exp2f(m0 - bs0), al1 = exp2f(m1 - bs1);
+      const float p0 = exp2f(x0 - bs0), p1 = exp2f(x1 - bs1), p2 = exp2f(x2 - bs0), p3 = exp2f(x3 - bs1);
+      l0 = l0 * al0 + (p0 + p2);
+      l1 = l1 * al1 + (p1 + p3);
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        oacc[mt][0] *= al0;
+        oacc[mt][1] *= al1;
+        oacc[mt][2] *= al0;
+        oacc[mt][3] *= al1;
+      }
+      // P^T as the B operand (k = token, n = head column): hi and lo halves
+      const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
+      const __half h2 = __float2half_rn(p2), h3 = __float2half_rn(p3);
+      const uint32_t phi_top = pack_u16x2(__half_as_ushort(h0), __half_as_ushort(h1));
+      const uint32_t phi_bot = pack_u16x2(__half_as_ushort(h2), __half_as_ushort(h3));
+      const uint32_t plo_top = pack_half2(p0 - __half2float(h0), p1 - __half2float(h1));
+      const uint32_t plo_bot = pack_half2(p2 - __half2float(h2), p3 - __half2float(h3));
+      const uint32_t bh0 = movmatrix_trans(phi_top), bh1 = movmatrix_trans(phi_bot);
+      const uint32_t bl0 = movmatrix_trans(plo_top), bl1 = movmatrix_trans(plo_bot);
+
+      // ---- V tile: per-token LUT (row min(pos, t_cal - 1))
+      const uint16_t* vl;
+      if (pos0 >= Tc) {
+        vl = sm.vtail;
+      } else {
+        for (int i = lane; i < DS * NLV; i += 32) {
+          int r = i / NLV, c = i % NLV;
+          int pr = min(pos0 + r, Tc - 1);
+          ws.vlut[r * NLV + c] =
+              c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + pr) * p.sc.levels_v + c] : (uint16_t)0;
+        }
+        __syncwarp();
+        vl = ws.vlut + t * NLV;
+      }
+      {
+        const uint8_t* rowp = ws.raw[st] + DS * RBK + t * RBV + half * (RBV / 2);
+        if (BV == 4) {
+          uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
+          uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+          for (int w8 = 0; w8 < 8; ++w8) {
+            uint16_t v[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) v[jj] = vl[(wv[w8] >> (4 * jj)) & 15u];
+            uint4 o4 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
+                                  pack_u16x2(v[6], v[7]));
+            const int chunk = (8 * half + w8) ^ (t & 7);
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
+          }
+        } else {
+          uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              uint16_t v[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) v[jj] = vl[(wv[w4] >> (2 * (8 * hh + jj))) & 3u];
+              uint4 o4 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
+                                    pack_u16x2(v[6], v[7]));
+              const int chunk = (8 * half + 2 * w4 + hh) ^ (t & 7);
+              *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      for (uint32_t e = lane; e < cntv; e += 32) {
+        uint32_t en = e < ENTCAP ? ws.ent[st][1][e] : p.pool.arena[offv + e];
+        int et = (en >> 24) & 31, ed = (en >> 16) & 255;
+        if (et < DS && ed < DD) ws.tile[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
+        else set_err(p.err, HX_DEV_ERR_BOUNDS);
+      }
+      __syncwarp();
+
+      // ---- O^T += V^T . P^T  (128 channels x 8 head columns)
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        uint32_t a[4];
+        const int r = (lane & 7) + ((lane >> 4) & 1) * 8;
+        const int chunk = (2 * mt + ((lane >> 3) & 1)) ^ (r & 7);
+        ldmatrix_x4_trans(a, ws.tile + r * DD + chunk * 8);
+        mma_16816(oacc[mt], a, bh0, bh1);
+        mma_16816(oacc[mt], a, bl0, bl1);
+      }
+      __syncwarp();
+      dcur = dn1;
+      dn1 = dn2;
+    }
+    if (timed_out) {
+      // give copies still in flight one more bounded wait before the buffers
+      // are reused, then stop this warp's work
+      for (int st = 0; st < 2; ++st)
+        if ((inflight >> st) & 1u && mbar_wait(&ws.bar[st], (phase >> st) & 1u)) {
+          phase ^= 1u << st;
+          inflight &= ~(1u << st);
+        }
+    }
+    __syncthreads();
+  }
+
+  // ---- warp -> CTA merge (smem reuses the stage buffers)
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 4);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 8);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 16);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 8);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
+  float* wO = reinterpret_cast<float*>(ws.raw);     // [8][128] floats = 4 KB
+  float* wml = reinterpret_cast<float*>(ws.vlut);   // m[8], l[8]
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int d = 16 * mt + g;
+    wO[(2 * qd) * DD + d] = oacc[mt][0];
+    wO[(2 * qd + 1) * DD + d] = oacc[mt][1];
+    wO[(2 * qd) * DD + d + 8] = oacc[mt][2];
+    wO[(2 * qd + 1) * DD + d + 8] = oacc[mt][3];
+  }
+  if (g == 0) {
+    wml[2 * qd] = m0;
+    wml[2 * qd + 1] = m1;
+    wml[8 + 2 * qd] = l0;
+    wml[8 + 2 * qd + 1] = l1;
+  }
+  __syncthreads();
+  float* mypart = p.part + ((int64_t)bh * p.n_splits + split) * PSZ;
+  {
+    const int d = tid;  // 128 threads = 128 channels
+    for (int c = 0; c < G; ++c) {
+      float M = -INFINITY;
+      for (int w = 0; w < NW; ++w) M = fmaxf(M, reinterpret_cast<float*>(sm.w[w].vlut)[c]);
+      const float base = M == -INFINITY ? 0.0f : M;
+      float L = 0.0f, O = 0.0f;
+      for (int w = 0; w < NW; ++w) {
+        const float* ml = reinterpret_cast<float*>(sm.w[w].vlut);
+        const float sc = exp2f(ml[c] - base);
+        L += sc * ml[8 + c];
+        O += sc * reinterpret_cast<float*>(sm.w[w].raw)[c * DD + d];
+      }
+      mypart[c * DD + d] = O;
+      if (d == 0) {
+        mypart[8 * DD + c] = M;
+        mypart[8 * DD + 8 + c] = L;
+      }
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) sm.last = (atomicAdd(&p.ctr[bh], 1u) == (uint32_t)(p.n_splits - 1));
+  __syncthreads();
+  if (!sm.last) return;
+  __threadfence();
+
+  // ---- last CTA of (b, h): merge the splits, normalise, write o / lse
+  const float* parts = p.part + (int64_t)bh * p.n_splits * PSZ;
+  const int d = tid;
+  for (int c = 0; c < G; ++c) {
+    float M = -INFINITY;
+    for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, __ldcg(parts + (int64_t)s * PSZ + 8 * DD + c));
+    const float base = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < p.n_splits; ++s) {
+      const float* ps = parts + (int64_t)s * PSZ;
+      const float sc = exp2f(__ldcg(ps + 8 * DD + c) - base);
+      L += sc * __ldcg(ps + 8 * DD + 8 + c);
+      O += sc * __ldcg(ps + c * DD + d);
+    }
+    const int64_t row = (int64_t)b * H * G + (int64_t)h * G + c;
+    const float ov = L > 0.0f ? O / L : 0.0f;
+    p.o[row * DD + d] = ov;
+    if (p.out16) p.out16[row * DD + d] = f2h(ov);
+    if (d == 0) p.lse[row] = L > 0.0f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+  }
+  if (tid == 0) p.ctr[bh] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// cross-shard merge of normalised (o, lse)
+
+__global__ void merge_kernel(const float* o_parts, const float* lse_parts, int R, int N, int D, float* o, float* lse,
+                             uint16_t* out16) {
+  const int i = blockIdx.x;
+  float M = -INFINITY;
+  for (int r = 0; r < R; ++r) M = fmaxf(M, lse_parts[(int64_t)r * N + i]);
+  const float base = M == -INFINITY ? 0.0f : M;
+  float W = 0.0f;
+  for (int r = 0; r < R; ++r) W += expf(lse_parts[(int64_t)r * N + i] - base);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int r = 0; r < R; ++r) {
+      float w = expf(lse_parts[(int64_t)r * N + i] - base);
+      if (w > 0.0f) acc += w * o_parts[((int64_t)r * N + i) * D + d];
+    }
+    float v = W > 0.0f ? acc / W : 0.0f;
+    o[(int64_t)i * D + d] = v;
+    if (out16) out16[(int64_t)i * D + d] = f2h(v);
+  }
+  if (threadIdx.x == 0) lse[i] = W > 0.0f ? base + logf(W) : -INFINITY;
+}
+
+// ---------------------------------------------------------------------------
+// dense selected_attention (fp32 CUDA cores): one block per query head
+
+template <typename TD>
+HX_DEVINL float ldx(const TD* p, int64_t i);
+template <>
+HX_DEVINL float ldx<float>(const float* p, int64_t i) { return p[i]; }
+template <>
+HX_DEVINL float ldx<uint16_t>(const uint16_t* p, int64_t i) { return h2f(p[i]); }
+
+template <typename TD>
+__global__ void selected_attention_kernel(const TD* q, const TD* K, const TD* V, const int64_t* idx, int k, int P,
+                                          int S, int H, int Hq, int D, float scale, TD* out) {
+  extern __shared__ float sh[];  // per warp: o[D]; then m, l per warp
+  const int i = blockIdx.x;
+  const int G = Hq / H;
+  const int kv = i / G;
+  const int warp = threadIdx.x >> 5, lane = lane_id(), nw = blockDim.x >> 5;
+  float m = -INFINITY, l = 0.0f;
+  float acc[8];  // D <= 256: 8 channels per lane
+#pragma unroll
+  for (int v = 0; v < 8; ++v) acc[v] = 0.0f;
+  const int ntok = k * S;
+  for (int tt = warp; tt < ntok; tt += nw) {
+    const int64_t pg = idx[(int64_t)(tt / S) * H + kv];
+    if (pg < 0 || pg >= P) continue;
+    const int64_t row = ((pg * S + tt % S) * H + kv) * D;
+    float s = 0.0f;
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      int d = lane + 32 * v;
+      if (d < D) s += ldx(q, (int64_t)i * D + d) * ldx(K, row + d);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    s *= scale;
+    const float mn = fmaxf(m, s);
+    const float al = expf(m - mn), pw = expf(s - mn);
+    l = l * al + pw;
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      int d = lane + 32 * v;
+      acc[v] = acc[v] * al + (d < D ? pw * ldx(V, row + d) : 0.0f);
+    }
+    m = mn;
+  }
+  float* wo = sh + warp * D;
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+    int d = lane + 32 * v;
+    if (d < D) wo[d] = acc[v];
+  }
+  float* wm = sh + nw * D;
+  if (lane == 0) {
+    wm[warp] = m;
+    wm[nw + warp] = l;
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float M = -INFINITY;
+    for (int w = 0; w < nw; ++w) M = fmaxf(M, wm[w]);
+    float L = 0.0f, O = 0.0f;
+    for (int w = 0; w < nw; ++w) {
+      float sc = wm[w] == -INFINITY ? 0.0f : expf(wm[w] - M);
+      L += sc * wm[nw + w];
+      O += sc * sh[w * D + d];
+    }
+    float v = L > 0.0f ? O / L : 0.0f;
+    if (sizeof(TD) == 4) reinterpret_cast<float*>(out)[(int64_t)i * D + d] = v;
+    else reinterpret_cast<uint16_t*>(out)[(int64_t)i * D + d] = f2h(v);
+  }
+}
+
+}  // namespace hx
+
+// ===========================================================================
+// C ABI
+
+using namespace hx;
+
+static inline cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+template <int BK, int BV>
+static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
+  const size_t smem = sizeof(CtaSmem);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_ERR_LAUNCH;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(decode_kernel<BK, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return HX_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  dim3 grid(p.n_splits, H, p.B);
+  decode_kernel<BK, BV><<<grid, NW * 32, smem, s>>>(p);
+  HX_LAUNCH_CHECK();
+  return HX_OK;
+}
+
+extern "C" {
+
+HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits) {
+  if (B <= 0 || H <= 0 || n_splits <= 0) return 0;
+  int64_t parts = (int64_t)B * H * n_splits * PSZ * (int64_t)sizeof(float);
+  int64_t ctr = (((int64_t)B * H * sizeof(uint32_t)) + 255) & ~255ll;
+  return ((parts + 255) & ~255ll) + ctr;
+}
+
+HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc, const uint16_t* q,
+                          int32_t B, int32_t group, float softmax_scale, const int32_t* block_table,
+                          int32_t bt_stride, const int32_t* seq_lens, int32_t page_begin, int32_t max_pages,
+                          int32_t sel_mode, const float* scores, const uint64_t* thresh, int32_t sink_pages,
+                          const int32_t* lists, int32_t list_stride, const int32_t* list_counts, int32_t n_splits,
+                          void* scratch, float* o, float* lse, uint16_t* out16, uint32_t* dev_err) {
+  if (!pool || !sc || !q || !seq_lens || !o || !lse || !scratch) return HX_ERR_ARG;
+  if (B < 0 || group <= 0 || n_splits <= 0 || max_pages < 0 || page_begin < 0) return HX_ERR_ARG;
+  if (B == 0) return HX_OK;
+  if (pool->head_size != DD || pool->block_size != DS || group > 8) return HX_ERR_UNSUPPORTED;
+  if ((pool->bits_k != 2 && pool->bits_k != 4) || (pool->bits_v != 2 && pool->bits_v != 4)) return HX_ERR_ARG;
+  if (sc->levels_k > (1 << pool->bits_k) || sc->levels_v > (1 << pool->bits_v) || sc->t_cal < 1) return HX_ERR_ARG;
+  if (sel_mode == HX_SEL_THRESHOLD && (!scores || !thresh)) return HX_ERR_ARG;
+  if (sel_mode == HX_SEL_LIST && (!lists || !list_counts || list_stride <= 0)) return HX_ERR_ARG;
+  if (sel_mode < 0 || sel_mode > 2) return HX_ERR_ARG;
+  if (block_table && bt_stride < max_pages) return HX_ERR_ARG;
+  DecodeParams p;
+  p.pool = *pool;
+  p.sc = *sc;
+  p.q = q;
+  p.B = B;
+  p.G = group;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.bt = block_table;
+  p.bt_stride = bt_stride;
+  p.seq_lens = seq_lens;
+  p.page_begin = page_begin;
+  p.max_pages = max_pages;
+  p.sel_mode = sel_mode;
+  p.scores = scores;
+  p.thresh = thresh;
+  p.sinks_req = sink_pages;
+  p.lists = lists;
+  p.list_stride = list_stride;
+  p.list_counts = list_counts;
+  p.n_splits = n_splits;
+  int64_t parts = (int64_t)B * pool->num_kv_heads * n_splits * PSZ * (int64_t)sizeof(float);
+  p.part = reinterpret_cast<float*>(scratch);
+  p.ctr = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(scratch) + ((parts + 255) & ~255ll));
+  p.o = o;
+  p.lse = lse;
+  p.out16 = out16;
+  p.err = dev_err;
+  cudaStream_t s = S_(stream);
+  const int H = pool->num_kv_heads;
+  if (pool->bits_k == 4 && pool->bits_v == 4) return launch_decode<4, 4>(p, H, s);
+  if (pool->bits_k == 4 && pool->bits_v == 2) return launch_decode<4, 2>(p, H, s);
+  if (pool->bits_k == 2 && pool->bits_v == 4) return launch_decode<2, 4>(p, H, s);
+  return launch_decode<2, 2>(p, H, s);
+}
+
+HX_API int hx_merge_partials(void* stream, const float* o_parts, const float* lse_parts, int32_t R, int32_t N,
+                             int32_t D, float* o, float* lse, uint16_t* out16) {
+  if (R <= 0 || N < 0 || D <= 0) return HX_ERR_ARG;
+  if (N == 0) return HX_OK;
+  if (!o_parts || !lse_parts || !o || !lse) return HX_ERR_ARG;
+  merge_kernel<<<N, 128, 0, S_(stream)>>>(o_parts, lse_parts, R, N, D, o, lse, out16);
+  HX_LAUNCH_CHECK();
+  return HX_OK;
+}
+
+HX_API int hx_selected_attention(void* stream, int32_t dtype, const void* q, const void* k_pages,
+                                 const void* v_pages, const int64_t* page_idx, int32_t k, int32_t P, int32_t S,
+                                 int32_t H, int32_t Hq, int32_t D, float softmax_scale, void* out) {
+  if ((dtype != 0 && dtype != 1) || k < 0 || P < 0 || S <= 0 || H <= 0 || Hq <= 0 || Hq % H != 0 || D <= 0 ||
+      D > 256)
+    return HX_ERR_ARG;
+  if (Hq == 0) return HX_OK;
+  if (!q || !out || (k > 0 && (!k_pages || !v_pages || !page_idx))) return HX_ERR_ARG;
+  const int threads = 256;
+  size_t smem = (size_t)(threads / 32) * D * sizeof(float) + 2 * (threads / 32) * sizeof(float);
+  if (dtype == 0)
+    selected_attention_kernel<float><<<Hq, threads, smem, S_(stream)>>>(
+        (const float*)q, (const float*)k_pages, (const float*)v_pages, page_idx, k, P, S, H, Hq, D, softmax_scale,
+        (float*)out);
+  else
+    selected_attention_kernel<uint16_t><<<Hq, threads, smem, S_(stream)>>>(
+        (const uint16_t*)q, (const uint16_t*)k_pages, (const uint16_t*)v_pages, page_idx, k, P, S, H, Hq, D,
+        softmax_scale, (uint16_t*)out);
+  HX_LAUNCH_CHECK();
+  return HX_OK;
+}
+
+}  // extern "C"

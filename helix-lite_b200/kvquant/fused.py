@@ -1,0 +1,176 @@
+"""Quest page selection and fused-dequant decode attention over a CompactKVPool.
+
+This is the B200 hot path that replaces, per layer and decode step,
+``select_top_blocks_for_layer`` + ``unpack_to_staging`` + FlashAttention on a
+fp16 staging buffer (src/kvquant/compact_backend.py:225-299):
+
+  quest_select   page scores from the pool's fp16 K min / max (pinned fp32
+                 arithmetic) and an exact per-(sequence, KV head) top-K
+                 threshold: sinks + the best k pages, ties to the lower page
+  decode         one decode token per sequence: the selected pages are read
+                 as packed codes, dequantised on chip and attended; returns
+                 normalised o (fp32) and lse (natural log)
+  selected_lists the selection as ascending page lists (API / tests)
+
+Everything is asynchronous on the current stream; scratch is cached per
+device and left zeroed by the kernels.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+import hxlib
+from hxlib import SEL_DENSE, SEL_LIST, SEL_THRESHOLD, call, ptr, stream
+
+from .compact_pool import CompactKVPool, ctypes_ref
+
+NUM_SMS = 148
+
+
+@dataclass
+class Selection:
+    scores: torch.Tensor      # (B, H, max_pages) fp32
+    thresh: torch.Tensor      # (B * H,) int64 holding uint64 thresholds
+    seq_lens: torch.Tensor    # (B,) int32 tokens
+    page_size: int
+    max_pages: int
+    sink_pages: int
+
+
+def _i32(t, device):
+    return t.to(device=device, dtype=torch.int32).contiguous()
+
+
+def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
+                 seq_lens: torch.Tensor, *, top_k: int | None = None, top_frac=(1, 4), sink_pages: int = 4,
+                 gqa: str = "sum", max_pages: int | None = None, scores: torch.Tensor | None = None,
+                 thresh: torch.Tensor | None = None) -> Selection:
+    """Score every page of each sequence and fix the exact top-K thresholds.
+
+    query (B, Hq, D) fp16 with Hq = group * H; block_table (B, >= max_pages)
+    logical -> pool page; seq_lens (B,) tokens; optional preallocated
+    ``scores`` (B, H, max_pages) fp32 and ``thresh`` (B*H,) int64 outputs.
+    Block table:
+    logical -> pool page; seq_lens (B,) tokens. k = top_k pages if given,
+    else floor(n_pages * top_frac[0] / top_frac[1]); gqa "sum" adds the
+    per-query-head bounds of a group, "mean" bounds the group's mean query
+    (the reference hook, compact_backend.py:231).
+    """
+    dev = pool.device
+    q = query.to(device=dev, dtype=torch.float16).contiguous()
+    B, Hq, D = q.shape
+    H = pool.num_kv_heads
+    S = pool.block_size
+    if Hq % H:
+        raise ValueError("query heads must be a multiple of KV heads")
+    bt = _i32(block_table, dev)
+    sl = _i32(seq_lens, dev)
+    mp = int(max_pages if max_pages is not None else bt.shape[1])
+    lay = pool.layers[layer_idx]
+    if scores is None:
+        scores = torch.empty((B, H, max(mp, 1)), dtype=torch.float32, device=dev)
+    if thresh is None:
+        thresh = torch.empty((B * H,), dtype=torch.int64, device=dev)
+    hist = hxlib.scratch(dev, "quest_hist", B * H * 4096 * 4)
+    cand = hxlib.scratch(dev, "quest_cand", B * H * max(mp, 1) * 8)
+    ctr = hxlib.scratch(dev, "quest_ctr", B * H * 2 * 4)
+    stats = lay.stats
+    with torch.cuda.device(dev):
+        st = stream(dev)
+        call("hx_quest_scores", st, ptr(q), B, H, Hq // H, D, 0 if gqa == "sum" else 1, 1,
+             ptr(stats), hxlib.ctypes.c_void_p(stats.data_ptr() + 2 * D), 2 * D, pool.num_blocks * 2 * D,
+             ptr(bt), bt.shape[1], ptr(sl), S, mp, sink_pages, ptr(scores), ptr(hist))
+        kf, fn, fd = (int(top_k), 0, 0) if top_k is not None else (0, int(top_frac[0]), int(top_frac[1]))
+        call("hx_quest_threshold", st, ptr(scores), B, H, ptr(sl), S, mp, sink_pages, kf, fn, fd, 1, ptr(hist),
+             ptr(cand), ptr(ctr), ptr(thresh), ptr(hxlib.err_word(dev)))
+    return Selection(scores, thresh, sl, S, mp, sink_pages)
+
+
+def selected_lists(sel: Selection, union: bool = False, max_out: int | None = None):
+    """Ascending selected logical pages: (B, H, max_out) int32 + counts (B, H);
+    with union=True the union over heads: (B, max_out) + (B,)."""
+    B, H, mp = sel.scores.shape
+    mo = int(max_out if max_out is not None else mp)
+    dev = sel.scores.device
+    rows = B if union else B * H
+    out = torch.full((rows, max(mo, 1)), -1, dtype=torch.int32, device=dev)
+    counts = torch.empty((rows,), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        call("hx_quest_compact", stream(dev), ptr(sel.scores), ptr(sel.thresh), B, H, ptr(sel.seq_lens),
+             sel.page_size, sel.max_pages, sel.sink_pages, 1 if union else 0, mo, ptr(out), ptr(counts))
+    if union:
+        return out, counts
+    return out.view(B, H, -1), counts.view(B, H)
+
+
+def default_splits(B: int, H: int, max_pages: int) -> int:
+    want = max(1, math.ceil(4 * NUM_SMS / max(1, B * H)))
+    return max(1, min(want, max(1, max_pages // 8)))
+
+
+def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
+           seq_lens: torch.Tensor, selection: Selection | None = None, *, lists: torch.Tensor | None = None,
+           list_counts: torch.Tensor | None = None, page_begin: int = 0, max_pages: int | None = None,
+           n_splits: int | None = None, softmax_scale: float | None = None, out16: torch.Tensor | None = None,
+           o: torch.Tensor | None = None, lse: torch.Tensor | None = None):
+    """Fused-dequant decode attention; returns (o (B, Hq, D) fp32, lse (B, Hq)).
+
+    Pages attended: every page (no selection), the Quest selection, or
+    explicit per-(b, h) logical page lists (``lists`` (B, H, L) int32 with
+    ``list_counts`` (B, H)). ``page_begin`` is the absolute logical page of
+    this pool's page 0 (split-KV shards), used for V's position clamp.
+    """
+    dev = pool.device
+    q = query.to(device=dev, dtype=torch.float16).contiguous()
+    B, Hq, D = q.shape
+    H = pool.num_kv_heads
+    bt = _i32(block_table, dev)
+    sl = _i32(seq_lens, dev)
+    mp = int(max_pages if max_pages is not None else bt.shape[1])
+    if selection is not None:
+        mode = SEL_THRESHOLD
+    elif lists is not None:
+        mode = SEL_LIST
+    else:
+        mode = SEL_DENSE
+    ns = int(n_splits or default_splits(B, H, mp if mode != SEL_LIST else lists.shape[-1]))
+    scale = float(softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D))
+    if o is None:
+        o = torch.empty((B, Hq, D), dtype=torch.float32, device=dev)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=dev)
+    nbytes = hxlib.lib().hx_decode_scratch_bytes(B, H, ns)
+    scr = hxlib.scratch(dev, "decode", nbytes)
+    st_scales, _keep = pool.scales.device_layer(layer_idx, dev)
+    if mode == SEL_LIST:
+        lists_c = _i32(lists, dev).view(B * H, -1)
+        counts_c = _i32(list_counts, dev)
+        lstride = lists_c.shape[1]
+    else:
+        lists_c = counts_c = None
+        lstride = 0
+    with torch.cuda.device(dev):
+        call("hx_decode_attn", stream(dev), ctypes_ref(pool.layers[layer_idx].struct), ctypes_ref(st_scales),
+             ptr(q), B, Hq // H, scale, ptr(bt), bt.shape[1], ptr(sl), int(page_begin), mp, mode,
+             ptr(selection.scores) if selection is not None else None,
+             ptr(selection.thresh) if selection is not None else None,
+             selection.sink_pages if selection is not None else 0,
+             ptr(lists_c), lstride, ptr(counts_c), ns, ptr(scr), ptr(o), ptr(lse), ptr(out16),
+             ptr(hxlib.err_word(dev)))
+    return o, lse
+
+
+def merge_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, out16: torch.Tensor | None = None):
+    """Merge R shards' normalised (o, lse): (R, N, D), (R, N) -> (N, D), (N,)."""
+    R, N, D = o_parts.shape
+    dev = o_parts.device
+    op = o_parts.to(torch.float32).contiguous()
+    lp = lse_parts.to(torch.float32).contiguous()
+    o = torch.empty((N, D), dtype=torch.float32, device=dev)
+    lse = torch.empty((N,), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        call("hx_merge_partials", stream(dev), ptr(op), ptr(lp), R, N, D, ptr(o), ptr(lse), ptr(out16))
+    return o, lse

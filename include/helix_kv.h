@@ -1,0 +1,265 @@
+/*
+ * helix_kv.h - C ABI of the B200 (sm_100a) long-context KV hot path.
+ *
+ * Plain C: pointers, sizes and status codes only. Every entry point is
+ * asynchronous on the CUDA stream it is given (a cudaStream_t passed as
+ * void*), allocates nothing, and returns HX_OK (0) when the launch was
+ * accepted or a nonzero HX_ERR_* for invalid arguments. Faults found on the
+ * device (a full outlier arena, an out-of-range index, a wait that ran out)
+ * are OR-ed into the caller's device word `dev_err` as HX_DEV_ERR_* bits;
+ * read it after synchronising.
+ *
+ * Pointers marked "device" are device memory. fp16 data is passed as
+ * uint16_t bit patterns.
+ *
+ * Reference interfaces replaced (paths inside xFuzzitx/helix-lite):
+ *   src/kvquant/compact_pool.py   CompactKVPool.write_kv / unpack_to_staging
+ *   src/kvquant/triton_batched.py pack_/unpack_{keys_per_channel,values_per_token}_batched
+ *   src/kvquant/nuq.py            quantize_nuq / dequantize_nuq (torch spec)
+ *   src/quest/reference.py        compute_page_stats / page_upper_bound /
+ *                                 topk_pages_with_sinks / selected_attention
+ *   src/quest/triton_kernels.py   page_upper_bound_triton
+ *   src/kvquant/quest_selector.py select_top_blocks_for_layer
+ *   src/kvquant/compact_backend.py KVQuantCompactImpl.forward (staging + FA)
+ */
+#ifndef HELIX_KV_H
+#define HELIX_KV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define HX_API __attribute__((visibility("default")))
+#else
+#define HX_API
+#endif
+
+/* host status codes */
+#define HX_OK              0
+#define HX_ERR_ARG         1   /* shape, pointer or size rejected */
+#define HX_ERR_UNSUPPORTED 2   /* valid request this build has no kernel for */
+#define HX_ERR_LAUNCH      3   /* the CUDA launch itself failed */
+
+/* device error bits, OR-ed into *dev_err */
+#define HX_DEV_ERR_ARENA_FULL 0x1u  /* outlier arena exhausted: entries dropped */
+#define HX_DEV_ERR_BOUNDS     0x2u  /* an index (page, slot, level) out of range */
+#define HX_DEV_ERR_TIMEOUT    0x4u  /* a bounded wait on a bulk copy ran out */
+#define HX_DEV_ERR_SELECT     0x8u  /* selection could not isolate a threshold */
+
+/* Calibrated nuq scales of one layer (src/kvquant/scales.py:14-70). */
+typedef struct hx_layer_scales {
+  const uint16_t* k_poles;   /* device fp16 (H, D, levels_k): per channel   */
+  const uint16_t* k_upper;   /* device fp16 (H, D)                          */
+  const uint16_t* k_lower;   /* device fp16 (H, D)                          */
+  const uint16_t* v_poles;   /* device fp16 (H, t_cal, levels_v): per token */
+  const uint16_t* v_upper;   /* device fp16 (H, t_cal)                      */
+  const uint16_t* v_lower;   /* device fp16 (H, t_cal)                      */
+  int32_t levels_k;          /* 2..16 */
+  int32_t levels_v;          /* 2..16 */
+  int32_t t_cal;             /* V positions >= t_cal use row t_cal - 1     */
+  int32_t reserved;
+} hx_layer_scales;
+
+/*
+ * One layer of the compact paged pool. Codes of a (head, page) live in one
+ * contiguous segment: K rows (S x D*bits_k/8 bytes) then V rows
+ * (S x D*bits_v/8). A row packs channel codes little-end first: nuq4 byte i
+ * = c[2i] | c[2i+1] << 4, nuq2 byte i = c[4i] | c[4i+1] << 2 | c[4i+2] << 4
+ * | c[4i+3] << 6. Outliers are sparse: every (head, page, K|V) has a
+ * directory record {offset, capacity, count, rows} into the layer's arena
+ * of 32-bit entries (bits 0-15 fp16 value, 16-23 channel, 24-28 slot).
+ */
+typedef struct hx_pool_layer {
+  uint8_t*  codes;         /* device (H, NB, seg_bytes)                     */
+  uint16_t* stats;         /* device fp16 (H, NB, 2, D): K min, K max       */
+  uint32_t* dir;           /* device (H, NB, 2, 4)                          */
+  uint32_t* arena;         /* device (arena_capacity,) outlier entries      */
+  uint32_t* arena_top;     /* device, one counter: entries handed out       */
+  int64_t   arena_capacity;
+  int32_t   num_blocks;    /* NB */
+  int32_t   block_size;    /* S, tokens per page, 1..32 */
+  int32_t   num_kv_heads;  /* H */
+  int32_t   head_size;     /* D, multiple of 8, <= 256 */
+  int32_t   bits_k;        /* 2 or 4 */
+  int32_t   bits_v;        /* 2 or 4 */
+} hx_pool_layer;
+
+/* ---- pool maintenance ------------------------------------------------- */
+
+/* Set every page of the layer to empty: stats to +inf / -inf, directory
+ * records to zero, arena counter to zero. Replaces the allocation-time
+ * initialisation of CompactKVPool.__post_init__ (compact_pool.py:418-444). */
+HX_API int hx_pool_init(void* stream, const hx_pool_layer* pool);
+
+/* Empty the listed pages (stats and outlier lists) so they can be reused. */
+HX_API int hx_pool_reset_pages(void* stream, const hx_pool_layer* pool,
+                               const int32_t* pages, int32_t n, uint32_t* dev_err);
+
+/* ---- pack on write (Kernel A) ----------------------------------------- */
+
+/* Quantise, bit-pack and append T tokens of one layer: K per channel, V per
+ * token at position min(abs_positions[t], t_cal - 1); outliers (outside the
+ * band) appended to the page lists; K page stats updated with the running
+ * min / max of the reconstructed K. slot_mapping[t] < 0 skips the token.
+ * Replaces CompactKVPool.write_kv (compact_pool.py:447-489). */
+HX_API int hx_pack_append(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
+                          const uint16_t* key, const uint16_t* value,      /* (T, H, D) fp16 */
+                          const int64_t* slot_mapping, const int64_t* abs_positions,
+                          int32_t T, uint32_t* dev_err);
+
+/* Dequantise whole pages to fp16 staging (NK, S, H, D) for K and V.
+ * Replaces CompactKVPool.unpack_to_staging (compact_pool.py:492-537). */
+HX_API int hx_unpack_pages(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
+                           const int64_t* block_ids, const int64_t* first_pos, int32_t nk,
+                           uint16_t* staging_k, uint16_t* staging_v, uint32_t* dev_err);
+
+/* ---- dense quantisation (the batched Triton API) ---------------------- */
+
+/* mode 0: K, poles (H, D, L), thresholds (H, D); mode 1: V, poles (H, T, L),
+ * thresholds (H, T). values (T, H, D) fp16 -> codes u8, outlier values fp16
+ * (0 elsewhere), outlier mask u8. Replaces pack_keys_per_channel_batched /
+ * pack_values_per_token_batched (triton_batched.py:125-148, :275-303). */
+HX_API int hx_nuq_pack_dense(void* stream, int32_t mode, const uint16_t* values,
+                             const uint16_t* poles, const uint16_t* upper, const uint16_t* lower,
+                             int32_t T, int32_t H, int32_t D, int32_t L,
+                             uint8_t* codes, uint16_t* outv, uint8_t* outm);
+
+/* Inverse of hx_nuq_pack_dense (triton_batched.py:151-171, :306-326). */
+HX_API int hx_nuq_unpack_dense(void* stream, int32_t mode, const uint8_t* codes,
+                               const uint16_t* outv, const uint8_t* outm, const uint16_t* poles,
+                               int32_t T, int32_t H, int32_t D, int32_t L, uint16_t* out);
+
+/* Flat quantise_nuq: n elements, poles (n, L) row-major, values and
+ * thresholds of one dtype (0 = fp32, 1 = fp16). Writes the reconstruction
+ * (same dtype) and the outlier mask (u8). Differences are taken in the
+ * input dtype as the torch spec does (nuq.py:22-38). Mask: the band test
+ * (nuq.py:72); with cap > 0 only the cap largest |normalised deviation|
+ * entries of each row of `row` elements stay (nuq.py:74-87, ties to the
+ * lower index); elements with (i / seq_stride) % seq_size < first_few are
+ * forced outliers (nuq.py:89-92). scratch_mask: n bytes, needed when cap > 0. */
+HX_API int hx_nuq_quantize_flat(void* stream, int32_t dtype, const void* values, const void* poles,
+                                const void* upper, const void* lower, int64_t n, int32_t L,
+                                int32_t cap, int64_t row, int64_t seq_stride, int64_t seq_size,
+                                int32_t first_few, void* recon, uint8_t* mask, uint8_t* scratch_mask);
+
+/* dequantize_nuq: out[i] = mask[i] ? outliers[i] : poles[i*L + codes[i]] in
+ * the dtype of outliers (nuq.py:135-156). codes are int64. */
+HX_API int hx_nuq_dequantize_flat(void* stream, int32_t dtype, const int64_t* codes,
+                                  const void* outliers, const uint8_t* mask, const void* poles,
+                                  int64_t n, int32_t L, void* out, uint32_t* dev_err);
+
+/* ---- Quest (Kernel B) -------------------------------------------------- */
+
+/* compute_page_stats: (P, S, H, D) -> min, max (P, H, D), dtype 0 fp32 / 1 fp16
+ * (quest/reference.py:38-56). */
+HX_API int hx_page_stats(void* stream, int32_t dtype, const void* k_pages,
+                         int32_t P, int32_t S, int32_t H, int32_t D, void* kmin, void* kmax);
+
+/*
+ * Page scores: for batch b, KV head h and logical page j < ceil(seq_lens[b]/S)
+ *   score = sum_d Qp[d] * kmax[d] + Qn[d] * kmin[d]
+ * with Qp / Qn the group terms of the `group` query heads of h (gqa_mode 0:
+ * sum of per-head clamps, 1: clamp of the fp16-rounded mean). Arithmetic
+ * order is pinned (32 lanes x ceil(D/32) channels, butterfly); products and
+ * sums are rounded to fp32 separately. Stats rows are addressed as
+ *   kmin + phys*page_stride + h*head_stride (same for kmax), phys =
+ *   block_table ? block_table[b*bt_stride + j] : j,
+ * with dtype 0 fp32 / 1 fp16. q is (B, H*group, D) fp16. Scores (B, H,
+ * max_pages) fp32. If hist != NULL, the top 12 bits of each non-sink page's
+ * order key are counted into hist (B*H, 4096), which must be zero on entry
+ * (hx_quest_threshold leaves it zero again).
+ * Replaces page_upper_bound / page_upper_bound_triton (reference.py:59-93,
+ * triton_kernels.py:26-91) and the GQA contraction (compact_backend.py:231).
+ */
+HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H, int32_t group,
+                           int32_t D, int32_t gqa_mode, int32_t stats_dtype,
+                           const void* kmin, const void* kmax, int64_t page_stride, int64_t head_stride,
+                           const int32_t* block_table, int32_t bt_stride,
+                           const int32_t* seq_lens, int32_t page_size, int32_t max_pages,
+                           int32_t sink_pages, float* scores, uint32_t* hist);
+
+/*
+ * Exact top-K threshold per (b, h): k_b = frac_den > 0 ? n_b*frac_num/frac_den
+ * : k_fixed pages, k_eff = min(k_b, n_b - sinks), sinks = min(sink_pages, n_b).
+ * Page j >= sinks is selected iff key64(j) >= thresh[b*H+h], key64 =
+ * order_key(score) << 32 | ~j; thresh = ~0 when k_eff == 0.
+ * Scratch: hist as above (filled by hx_quest_scores when hist_ready != 0,
+ * else counted here from `scores`); cand (B*H*max_pages) u64; counters
+ * (B*H*2) u32; all zero on entry and left zero. Replaces the torch.topk of
+ * topk_pages_with_sinks (reference.py:96-133) with a deterministic order.
+ */
+HX_API int hx_quest_threshold(void* stream, const float* scores, int32_t B, int32_t H,
+                              const int32_t* seq_lens, int32_t page_size, int32_t max_pages,
+                              int32_t sink_pages, int32_t k_fixed, int32_t frac_num, int32_t frac_den,
+                              int32_t hist_ready, uint32_t* hist, uint64_t* cand, uint32_t* counters,
+                              uint64_t* thresh, uint32_t* dev_err);
+
+/* Selected logical pages, ascending, per (b, h): out (B, H, max_out) int32
+ * and counts (B, H). union_heads != 0 writes the union over heads instead:
+ * out (B, max_out), counts (B). */
+HX_API int hx_quest_compact(void* stream, const float* scores, const uint64_t* thresh,
+                            int32_t B, int32_t H, const int32_t* seq_lens, int32_t page_size,
+                            int32_t max_pages, int32_t sink_pages, int32_t union_heads,
+                            int32_t max_out, int32_t* out, int32_t* counts);
+
+/* ---- fused-dequant decode attention (Kernel C) ------------------------ */
+
+#define HX_SEL_DENSE     0   /* every page of the sequence                  */
+#define HX_SEL_THRESHOLD 1   /* sinks + pages with key64 >= thresh          */
+#define HX_SEL_LIST      2   /* explicit per-(b, h) logical page lists      */
+
+/* Scratch bytes hx_decode_attn needs for B sequences, H heads, n_splits. */
+HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits);
+
+/*
+ * One decode token per sequence over the compact pool. q (B, H*group, D) fp16
+ * (group <= 8, D = 128, page_size = 16). Logical page j of sequence b is pool
+ * page block_table[b*bt_stride + j] and starts at absolute position
+ * (page_begin + j) * 16 (V tail clamp); tokens >= seq_lens[b] are masked.
+ * Selection: HX_SEL_DENSE; HX_SEL_THRESHOLD with scores / thresh from
+ * hx_quest_scores / hx_quest_threshold; HX_SEL_LIST with lists (B, H,
+ * list_stride) and list_counts (B, H). The sequence is split n_splits ways
+ * per (b, h); the last CTA of each (b, h) merges the splits. Writes o (B,
+ * H*group, D) fp32 normalised, lse (B, H*group) natural log (-inf for an
+ * empty selection), and out16 (same shape, fp16) when non-NULL. scratch:
+ * hx_decode_scratch_bytes bytes, zero on entry the first time; the kernel
+ * leaves its counters zero.
+ * Replaces unpack_to_staging + flash_attn_varlen_func in
+ * KVQuantCompactImpl.forward (compact_backend.py:233-299).
+ */
+HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
+                          const uint16_t* q, int32_t B, int32_t group, float softmax_scale,
+                          const int32_t* block_table, int32_t bt_stride, const int32_t* seq_lens,
+                          int32_t page_begin, int32_t max_pages, int32_t sel_mode,
+                          const float* scores, const uint64_t* thresh, int32_t sink_pages,
+                          const int32_t* lists, int32_t list_stride, const int32_t* list_counts,
+                          int32_t n_splits, void* scratch, float* o, float* lse, uint16_t* out16,
+                          uint32_t* dev_err);
+
+/* Merge R shards' (o, lse): o_parts (R, N, D) fp32, lse_parts (R, N) ->
+ * o (N, D) fp32, lse (N), out16 (N, D) fp16 if non-NULL. Used after the
+ * all-gather of split-KV partials across GPUs. */
+HX_API int hx_merge_partials(void* stream, const float* o_parts, const float* lse_parts,
+                             int32_t R, int32_t N, int32_t D, float* o, float* lse, uint16_t* out16);
+
+/*
+ * selected_attention on dense pages (quest/reference.py:136-168), fp32
+ * arithmetic, grouped-query: q (Hq, D), K / V pages (P, S, H, D) (dtype 0
+ * fp32 / 1 fp16), page_idx (k, H) int64 (column h: pages of KV head h).
+ * Query head i reads KV head i / (Hq / H). out (Hq, D) in the dtype of q.
+ */
+HX_API int hx_selected_attention(void* stream, int32_t dtype, const void* q, const void* k_pages,
+                                 const void* v_pages, const int64_t* page_idx, int32_t k,
+                                 int32_t P, int32_t S, int32_t H, int32_t Hq, int32_t D,
+                                 float softmax_scale, void* out);
+
+/* Library version and build arch string ("sm_100a"). */
+HX_API const char* hx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HELIX_KV_H */

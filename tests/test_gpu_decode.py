@@ -1,0 +1,203 @@
+"""GPU parity: Kernel C (fused-dequant split-KV decode) against fp64
+dequantise-then-attend on the oracle pool, within 2e-3 max-abs; and the
+cross-shard (o, lse) merge."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import make_pools, np16, write_both
+from oracle import attention as oatt
+from oracle import quest as oq
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3  # max-abs on the normalised attention output
+
+
+def _build(layout, n_tokens, seed, B=1, t_cal=4096, pages_extra=0, shuffle=False):
+    from kvquant.synthetic import make_kv, make_scales
+    H, D, S = 4, 128, 16
+    sc = make_scales(layout, H, D, t_cal=t_cal, seed=seed)
+    n_pages = [-(-n // S) for n in n_tokens]
+    NB = sum(n_pages) + pages_extra
+    gpu, orc = make_pools(sc, NB, S, H, D)
+    g = torch.Generator(device="cuda").manual_seed(seed + 1)
+    perm = torch.randperm(NB, generator=g, device="cuda") if shuffle else torch.arange(NB, device="cuda")
+    maxp = max(n_pages)
+    bt = torch.zeros((B, maxp), dtype=torch.int32, device="cuda")
+    base = 0
+    for b in range(B):
+        bt[b, :n_pages[b]] = perm[base:base + n_pages[b]].to(torch.int32)
+        base += n_pages[b]
+    for li, (levels, frac, side) in enumerate(layout):
+        for b in range(B):
+            K, V = make_kv(n_tokens[b], H, D, seed=seed + 10 * li + 100 * b, outlier_frac=frac)
+            pos = torch.arange(n_tokens[b], device="cuda")
+            slots = bt[b, pos // S].to(torch.int64) * S + pos % S
+            write_both(gpu, orc, li, K, V, slots, pos)
+    gpu.check()
+    return gpu, orc, bt, torch.tensor(n_tokens, dtype=torch.int32, device="cuda")
+
+
+def _oracle_out(orc, layer, q, bt, sl, pages_per_head=None):
+    B = q.shape[0]
+    outs, lses = [], []
+    for b in range(B):
+        n = int(sl[b])
+        K, V = orc.dequant_sequence(layer, np16(bt[b]), n)
+        mask = None
+        if pages_per_head is not None:
+            mask = oatt.page_mask_to_token_mask(pages_per_head[b], n, 16)
+        o, lse = oatt.decode_attention(np16(q[b]).astype(np.float64), K, V, mask)
+        outs.append(o)
+        lses.append(lse)
+    return np.stack(outs), np.stack(lses)
+
+
+def _query(B, G, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return torch.randn((B, 4 * G, 128), generator=g, device="cuda").to(torch.float16)
+
+
+@pytest.mark.parametrize("layout_name", ["nuq4", "nuq2"])
+def test_dense_decode_matches_oracle(layout_name):
+    from kvquant import fused
+    from kvquant.synthetic import NUQ2, NUQ4
+    layout = {"nuq4": [NUQ4], "nuq2": [NUQ2]}[layout_name]
+    gpu, orc, bt, sl = _build(layout, [5000 - 7], seed=20)
+    q = _query(1, 7, 21)
+    o, lse = fused.decode(gpu, 0, q, bt, sl)
+    gpu.check()
+    ro, rl = _oracle_out(orc, 0, q, bt, sl)
+    assert np.abs(np16(o) - ro).max() < TOL
+    np.testing.assert_allclose(np16(lse), rl, atol=1e-3)
+
+
+def test_quest_decode_matches_oracle_config3_shape():
+    """Config 3 shape at 16K context: nuq4 pool, Quest 25% + 4 sinks, G=7,
+    t_cal crossing (V per-token rows then the tail row)."""
+    from kvquant import fused
+    from kvquant.synthetic import NUQ4
+    gpu, orc, bt, sl = _build([NUQ4], [16384], seed=30, t_cal=4096)
+    q = _query(1, 7, 31)
+    sel = fused.quest_select(gpu, 0, q, bt, sl, top_frac=(1, 4), sink_pages=4)
+    o, lse = fused.decode(gpu, 0, q, bt, sl, sel)
+    lists, counts = fused.selected_lists(sel)
+    gpu.check()
+    n = 1024
+    kmin = orc.stats[0][:, :n, 0].transpose(1, 0, 2)
+    kmax = orc.stats[0][:, :n, 1].transpose(1, 0, 2)
+    qp, qn = oq.group_terms(np16(q[0]), 7, "sum")
+    ref = oq.page_scores(qp, qn, kmin, kmax)
+    pages = [oq.select_pages(ref[:, h], n // 4, 4) for h in range(4)]
+    for h in range(4):
+        np.testing.assert_array_equal(np16(lists[0, h, :int(counts[0, h])]), pages[h])
+    ro, rl = _oracle_out(orc, 0, q, bt, sl, [pages])
+    assert np.abs(np16(o) - ro).max() < TOL
+    np.testing.assert_allclose(np16(lse), rl, atol=1e-3)
+
+
+def test_batched_decode_block_tables_partial_pages():
+    """Config 4 flavour: several sequences of ragged lengths, shuffled pool
+    pages, partial last pages, a 1-token and an exactly-one-page sequence."""
+    from kvquant import fused
+    from kvquant.synthetic import NUQ4
+    lens = [1, 16, 777, 2048 + 5]
+    gpu, orc, bt, sl = _build([NUQ4], lens, seed=40, B=len(lens), shuffle=True, pages_extra=3)
+    q = _query(len(lens), 7, 41)
+    o, lse = fused.decode(gpu, 0, q, bt, sl, n_splits=5)
+    ro, rl = _oracle_out(orc, 0, q, bt, sl)
+    assert np.abs(np16(o) - ro).max() < TOL
+    sel = fused.quest_select(gpu, 0, q, bt, sl, top_frac=(1, 4), sink_pages=4)
+    lists, counts = fused.selected_lists(sel)
+    o2, _ = fused.decode(gpu, 0, q, bt, sl, sel, n_splits=3)
+    gpu.check()
+    pages = [[np16(lists[b, h, :int(counts[b, h])]) for h in range(4)] for b in range(len(lens))]
+    ro2, _ = _oracle_out(orc, 0, q, bt, sl, pages)
+    assert np.abs(np16(o2) - ro2).max() < TOL
+
+
+def test_list_mode_and_mixed_layers():
+    """Explicit page lists (the reference hook's per-head selection) on a
+    two-layer pool: nuq2 layer 0, nuq4 layer 1."""
+    from kvquant import fused
+    from kvquant.synthetic import NUQ2, NUQ4
+    gpu, orc, bt, sl = _build([NUQ2, NUQ4], [3000], seed=50)
+    q = _query(1, 7, 51)
+    rng = np.random.default_rng(52)
+    n = 188
+    per_head = [np.sort(rng.choice(n, size=40, replace=False)) for _ in range(4)]
+    lists = torch.tensor(np.stack(per_head), dtype=torch.int32, device="cuda").unsqueeze(0)
+    counts = torch.full((1, 4), 40, dtype=torch.int32, device="cuda")
+    for layer in (0, 1):
+        o, _ = fused.decode(gpu, layer, q, bt, sl, lists=lists, list_counts=counts)
+        ro, _ = _oracle_out(orc, layer, q, bt, sl, [per_head])
+        assert np.abs(np16(o) - ro).max() < TOL
+    gpu.check()
+
+
+def test_empty_selection_gives_zero_output():
+    from kvquant import fused
+    from kvquant.synthetic import NUQ4
+    gpu, orc, bt, sl = _build([NUQ4], [64], seed=60)
+    q = _query(1, 7, 61)
+    lists = torch.zeros((1, 4, 1), dtype=torch.int32, device="cuda")
+    counts = torch.zeros((1, 4), dtype=torch.int32, device="cuda")
+    o, lse = fused.decode(gpu, 0, q, bt, sl, lists=lists, list_counts=counts)
+    gpu.check()
+    assert float(o.abs().max()) == 0.0
+    assert torch.isinf(lse).all() and (lse < 0).all()
+
+
+def test_merge_partials_split_kv_equals_unsharded():
+    """Split-KV: shard a sequence's pages into 3 pools, decode each with its
+    page_begin, merge (o, lse): equal to the unsharded decode."""
+    from kvquant import fused
+    from kvquant.compact_pool import CompactKVPool
+    from kvquant.synthetic import NUQ4, make_kv, make_scales
+    H, D, S, n = 4, 128, 16, 4000
+    sc = make_scales([NUQ4], H, D, t_cal=1000, seed=70)
+    K, V = make_kv(n, H, D, seed=71)
+    q = _query(1, 7, 72)
+    full = CompactKVPool(1, 250, S, H, D, sc)
+    pos = torch.arange(n, device="cuda")
+    full.write_kv(0, K, V, pos, pos)
+    bt = torch.arange(250, dtype=torch.int32, device="cuda").unsqueeze(0)
+    o_ref, lse_ref = fused.decode(full, 0, q, bt, torch.tensor([n], dtype=torch.int32, device="cuda"))
+    bounds = oq.shard_bounds(250, 3)
+    os_, ls_ = [], []
+    for r in range(3):
+        a, b = bounds[r], bounds[r + 1]
+        shard = CompactKVPool(1, b - a, S, H, D, sc)
+        t0, t1 = a * S, min(b * S, n)
+        p = torch.arange(t1 - t0, device="cuda")
+        shard.write_kv(0, K[t0:t1].contiguous(), V[t0:t1].contiguous(), p, p + t0)
+        btr = torch.arange(b - a, dtype=torch.int32, device="cuda").unsqueeze(0)
+        o, lse = fused.decode(shard, 0, q, btr, torch.tensor([t1 - t0], dtype=torch.int32, device="cuda"),
+                              page_begin=a)
+        os_.append(o[0])
+        ls_.append(lse[0])
+    o_m, lse_m = fused.merge_partials(torch.stack(os_), torch.stack(ls_))
+    full.check()
+    assert float((o_m - o_ref[0]).abs().max()) < 1e-5
+    assert float((lse_m - lse_ref[0]).abs().max()) < 1e-5
+    ro, rl = oatt.merge_partials(np16(torch.stack(os_)), np16(torch.stack(ls_)))
+    np.testing.assert_allclose(np16(o_m), ro, atol=1e-6)
+
+
+def test_decode_scale_and_group_one():
+    """G = 1 (H == Hq, the reference's selected_attention shape) and a custom
+    softmax scale."""
+    from kvquant import fused
+    from kvquant.synthetic import NUQ4
+    gpu, orc, bt, sl = _build([NUQ4], [700], seed=80)
+    q = _query(1, 1, 81)
+    o, _ = fused.decode(gpu, 0, q, bt, sl, softmax_scale=0.05)
+    gpu.check()
+    K, V = orc.dequant_sequence(0, np16(bt[0]), 700)
+    ro, _ = oatt.decode_attention(np16(q[0]).astype(np.float64), K, V, scale=0.05)
+    assert np.abs(np16(o[0]) - ro).max() < TOL
