@@ -53,8 +53,7 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
     query (B, Hq, D) fp16 with Hq = group * H; block_table (B, >= max_pages)
     logical -> pool page; seq_lens (B,) tokens; optional preallocated
     ``scores`` (B, H, max_pages) fp32 and ``thresh`` (B*H,) int64 outputs.
-    Block table:
-    logical -> pool page; seq_lens (B,) tokens. k = top_k pages if given,
+    k = top_k pages if given,
     else floor(n_pages * top_frac[0] / top_frac[1]); gqa "sum" adds the
     per-query-head bounds of a group, "mean" bounds the group's mean query
     (the reference hook, compact_backend.py:231).
@@ -131,6 +130,7 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
     sl = _i32(seq_lens, dev)
     mp = int(max_pages if max_pages is not None else bt.shape[1])
     if selection is not None:
+        mp = selection.max_pages  # the scores' row stride
         mode = SEL_THRESHOLD
     elif lists is not None:
         mode = SEL_LIST
