@@ -254,6 +254,30 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
     if ((int)LVs.rows > t0) LVs.cnt = filter_slots(pool.arena, LVs.off, LVs.cnt, t0, t0 + n);
   }
 
+  // Count the run's outliers first and size the page lists once, so a
+  // prefill run allocates exactly what it needs (no growth copies).
+  {
+    uint32_t needk = 0, needv = 0;
+    for (int j = 0; j < n; ++j) {
+      const int64_t row = ((int64_t)(i + j) * H + h) * D;
+      int64_t p = abspos[i + j];
+      p = p < 0 ? 0 : p;
+      const int64_t prow = (int64_t)h * Tc + (p < Tc ? p : Tc - 1);
+      const float vup = h2f(sc.v_upper[prow]), vlo = h2f(sc.v_lower[prow]);
+#pragma unroll
+      for (int k = 0; k < KD; ++k) {
+        int d = lane + 32 * k;
+        bool ok = d < D;
+        float xk = ok ? h2f(key[row + d]) : 0.0f;
+        float xv = ok ? h2f(value[row + d]) : 0.0f;
+        needk += __popc(__ballot_sync(0xffffffffu, ok && ((xk > kup[k]) || (xk < klo[k]))));
+        needv += __popc(__ballot_sync(0xffffffffu, ok && ((xv > vup) || (xv < vlo))));
+      }
+    }
+    ensure_capacity(pool, LKs, LKs.cnt + needk, err);
+    ensure_capacity(pool, LVs, LVs.cnt + needv, err);
+  }
+
   for (int j = 0; j < n; ++j) {
     const int t = t0 + j;
     const int64_t row = ((int64_t)(i + j) * H + h) * D;

@@ -17,12 +17,14 @@ from .scales import KVScales, PerChannelScale, PerTokenScale
 
 
 def make_kv(T: int, H: int, D: int, seed: int, outlier_frac: float = 0.01, device="cuda",
-            chan_scale: torch.Tensor | None = None):
-    """(K, V) fp16 (T, H, D). ``chan_scale`` (2, H, D) fixes the per-channel
-    scales (so chunks of one sequence share them); default draws them."""
+            chan_scale: torch.Tensor | None = None, chan_seed: int | None = None):
+    """(K, V) fp16 (T, H, D) sampled with ``seed``. The per-channel scales
+    (2, H, D) are ``chan_scale`` if given, else drawn from ``chan_seed``
+    (default ``seed``); data meant for the scales of ``make_scales(seed=s)``
+    layer i uses chan_seed = s + 1000 * i."""
     g = torch.Generator(device=device).manual_seed(seed)
     if chan_scale is None:
-        chan_scale = channel_scales(H, D, seed, device)
+        chan_scale = channel_scales(H, D, seed if chan_seed is None else chan_seed, device)
     out = []
     for i in range(2):
         x = torch.randn((T, H, D), generator=g, device=device, dtype=torch.float32) * chan_scale[i]

@@ -35,7 +35,8 @@ def _build(layout, n_tokens, seed, B=1, t_cal=4096, pages_extra=0, shuffle=False
         base += n_pages[b]
     for li, (levels, frac, side) in enumerate(layout):
         for b in range(B):
-            K, V = make_kv(n_tokens[b], H, D, seed=seed + 10 * li + 100 * b, outlier_frac=frac)
+            K, V = make_kv(n_tokens[b], H, D, seed=seed + 10 * li + 100 * b, outlier_frac=frac,
+                           chan_seed=seed + 1000 * li)
             pos = torch.arange(n_tokens[b], device="cuda")
             slots = bt[b, pos // S].to(torch.int64) * S + pos % S
             write_both(gpu, orc, li, K, V, slots, pos)
@@ -161,7 +162,7 @@ def test_merge_partials_split_kv_equals_unsharded():
     from kvquant.synthetic import NUQ4, make_kv, make_scales
     H, D, S, n = 4, 128, 16, 4000
     sc = make_scales([NUQ4], H, D, t_cal=1000, seed=70)
-    K, V = make_kv(n, H, D, seed=71)
+    K, V = make_kv(n, H, D, seed=71, chan_seed=70)
     q = _query(1, 7, 72)
     full = CompactKVPool(1, 250, S, H, D, sc)
     pos = torch.arange(n, device="cuda")

@@ -135,7 +135,7 @@ def test_pool_incremental_appends_and_overwrite():
     H, D, S = 4, 128, 16
     sc = make_scales([NUQ2], H, D, t_cal=48, seed=3)
     gpu, orc = make_pools(sc, 12, S, H, D)
-    K, V = make_kv(200, H, D, seed=4, outlier_frac=0.05)
+    K, V = make_kv(200, H, D, seed=4, outlier_frac=0.05, chan_seed=3)
     # prefill 37 tokens from slot 5, then 20 single-token appends
     slots = torch.arange(5, 42, device="cuda")
     write_both(gpu, orc, 0, K[:37].contiguous(), V[:37].contiguous(), slots, slots)
@@ -169,7 +169,7 @@ def test_pool_reset_pages_empties_lists_and_stats():
     H, D, S = 4, 128, 16
     sc = make_scales([NUQ4], H, D, t_cal=64, seed=5)
     gpu, _ = make_pools(sc, 4, S, H, D)
-    K, V = make_kv(64, H, D, seed=6, outlier_frac=0.05)
+    K, V = make_kv(64, H, D, seed=6, outlier_frac=0.05, chan_seed=5)
     s = torch.arange(64, device="cuda")
     gpu.write_kv(0, K, V, s, s)
     gpu.reset_pages(0, torch.tensor([1, 2], device="cuda"))
