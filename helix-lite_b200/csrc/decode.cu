@@ -625,11 +625,16 @@ static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
 
 extern "C" {
 
+// Scratch layout: a fixed region of per-(b, h) split counters first (always
+// at offset 0, so counters never land where an earlier call with another
+// split count wrote partials), then the split partials.
+constexpr int64_t kCtrBytes = 64 * 1024;
+constexpr int64_t kMaxBH = kCtrBytes / 4;
+
 HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits) {
-  if (B <= 0 || H <= 0 || n_splits <= 0) return 0;
+  if (B <= 0 || H <= 0 || n_splits <= 0 || (int64_t)B * H > kMaxBH) return 0;
   int64_t parts = (int64_t)B * H * n_splits * PSZ * (int64_t)sizeof(float);
-  int64_t ctr = (((int64_t)B * H * sizeof(uint32_t)) + 255) & ~255ll;
-  return ((parts + 255) & ~255ll) + ctr;
+  return kCtrBytes + parts;
 }
 
 HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc, const uint16_t* q,
@@ -668,9 +673,9 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
   p.list_stride = list_stride;
   p.list_counts = list_counts;
   p.n_splits = n_splits;
-  int64_t parts = (int64_t)B * pool->num_kv_heads * n_splits * PSZ * (int64_t)sizeof(float);
-  p.part = reinterpret_cast<float*>(scratch);
-  p.ctr = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(scratch) + ((parts + 255) & ~255ll));
+  if ((int64_t)B * pool->num_kv_heads > kMaxBH) return HX_ERR_ARG;
+  p.ctr = reinterpret_cast<uint32_t*>(scratch);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCtrBytes);
   p.o = o;
   p.lse = lse;
   p.out16 = out16;

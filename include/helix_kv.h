@@ -225,8 +225,9 @@ HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits);
  * per (b, h); the last CTA of each (b, h) merges the splits. Writes o (B,
  * H*group, D) fp32 normalised, lse (B, H*group) natural log (-inf for an
  * empty selection), and out16 (same shape, fp16) when non-NULL. scratch:
- * hx_decode_scratch_bytes bytes, zero on entry the first time; the kernel
- * leaves its counters zero.
+ * hx_decode_scratch_bytes bytes: a 64 KB region of split counters (B*H <=
+ * 16384) that must be zero the first time and is left zero, then the split
+ * partials.
  * Replaces unpack_to_staging + flash_attn_varlen_func in
  * KVQuantCompactImpl.forward (compact_backend.py:233-299).
  */
