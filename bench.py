@@ -55,6 +55,18 @@ def parse():
     return ap.parse_args()
 
 
+def read_traffic(kernel):
+    """dram bytes per launch of `kernel` from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) == 2 and parts[0] == kernel and not line.startswith("#"):
+            return int(parts[1])
+    return None
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -375,13 +387,7 @@ def run_ours(args):
         dom_b = dec_b if dom == "decode" else sc_b
         dom_ms = dec_avg if dom == "decode" else sel_avg
         achieved = dom_b / (dom_ms * 1e-3) / 1e9
-        traffic = None
-        tf = ROOT / "profiles" / "traffic.json"
-        if tf.exists():
-            try:
-                traffic = json.loads(tf.read_text()).get(dom)
-            except Exception:
-                traffic = None
+        traffic = read_traffic(dom)
         res = {
             "metric": METRIC,
             "value": round(gbs, 2),
