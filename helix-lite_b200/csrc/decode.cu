@@ -688,6 +688,58 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
   return launch_decode<2, 2>(p, H, s);
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free decode: the same kernel with its scratch in a fixed device
+// array of this library. For callers that cannot call cudaMalloc: a serving
+// engine that reserves nearly all HBM for its own KV pool at start-up and
+// allows no allocation in its decode loop, or a foreign-language binding that
+// holds only raw device pointers and has no allocator to hand us a buffer
+// (cudaMalloc would also synchronise the device in the middle of a step).
+// Every GPU that loads this library holds the array until the process exits.
+
+constexpr int64_t kStaticMaxSplitRows = 1024;  // B * H * n_splits at most
+constexpr int64_t kStaticScratchBytes = kCtrBytes + kStaticMaxSplitRows * PSZ * (int64_t)sizeof(float);
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+static void* g_decode_scratch_addr[64];
+
+// The array's device address, looked up once per device with that device
+// current (host code may not use the symbol itself as a pointer).
+static int static_decode_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_ERR_LAUNCH;
+  if (!g_decode_scratch_addr[dev]) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_decode_scratch) != cudaSuccess || !addr) {
+      (void)cudaGetLastError();
+      return HX_ERR_LAUNCH;
+    }
+    g_decode_scratch_addr[dev] = addr;
+  }
+  *out = g_decode_scratch_addr[dev];
+  return HX_OK;
+}
+
+HX_API int hx_decode_attn_noalloc(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
+                                  const uint16_t* q, int32_t B, int32_t group, float softmax_scale,
+                                  const int32_t* block_table, int32_t bt_stride, const int32_t* seq_lens,
+                                  int32_t page_begin, int32_t max_pages, int32_t sel_mode, const float* scores,
+                                  const uint64_t* thresh, int32_t sink_pages, const int32_t* lists,
+                                  int32_t list_stride, const int32_t* list_counts, int32_t n_splits, float* o,
+                                  float* lse, uint16_t* out16, uint32_t* dev_err) {
+  if (!pool || B < 0 || n_splits <= 0) return HX_ERR_ARG;
+  if (B == 0) return HX_OK;
+  if ((int64_t)B * pool->num_kv_heads * n_splits > kStaticMaxSplitRows) return HX_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  int rc = static_decode_scratch(&scratch);
+  if (rc != HX_OK) return rc;
+  // the array keeps the previous call's contents: the split counters must start at zero
+  if (cudaMemsetAsync(scratch, 0, (size_t)B * pool->num_kv_heads * sizeof(uint32_t), S_(stream)) != cudaSuccess)
+    return HX_ERR_LAUNCH;
+  return hx_decode_attn(stream, pool, sc, q, B, group, softmax_scale, block_table, bt_stride, seq_lens, page_begin,
+                        max_pages, sel_mode, scores, thresh, sink_pages, lists, list_stride, list_counts, n_splits,
+                        scratch, o, lse, out16, dev_err);
+}
+
 HX_API int hx_merge_partials(void* stream, const float* o_parts, const float* lse_parts, int32_t R, int32_t N,
                              int32_t D, float* o, float* lse, uint16_t* out16) {
   if (R <= 0 || N < 0 || D <= 0) return HX_ERR_ARG;

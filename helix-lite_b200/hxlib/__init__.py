@@ -17,7 +17,7 @@ _HERE = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("HELIX_KV_LIB", _HERE / "libhelix_kv.so"))
 
 # status and device error bits (helix_kv.h)
-HX_OK, HX_ERR_ARG, HX_ERR_UNSUPPORTED, HX_ERR_LAUNCH = 0, 1, 2, 3
+HX_OK, HX_ERR_ARG, HX_ERR_UNSUPPORTED, HX_ERR_LAUNCH, HX_ERR_SCRATCH_LIMIT = 0, 1, 2, 3, 4
 DEV_ERR = {0x1: "outlier arena full", 0x2: "index out of range", 0x4: "bounded wait ran out",
            0x8: "selection threshold not isolated"}
 SEL_DENSE, SEL_THRESHOLD, SEL_LIST = 0, 1, 2
@@ -61,6 +61,9 @@ _SIGS = {
     "hx_decode_attn": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_i32, c_i32, c_f32, c_vp, c_i32,
                                c_vp, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_vp, c_i32, c_vp, c_i32,
                                c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "hx_decode_attn_noalloc": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_i32, c_i32, c_f32, c_vp,
+                                       c_i32, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_vp, c_i32, c_vp,
+                                       c_i32, c_vp, c_vp, c_vp, c_vp]),
     "hx_merge_partials": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]),
     "hx_selected_attention": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                                       c_i32, c_i32, c_f32, c_vp]),
@@ -98,7 +101,8 @@ def lib():
 LAUNCHES = {"hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 1, "hx_unpack_pages": 1,
             "hx_nuq_pack_dense": 1, "hx_nuq_unpack_dense": 1, "hx_nuq_quantize_flat": 2,
             "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": 1,
-            "hx_quest_compact": 1, "hx_decode_attn": 1, "hx_merge_partials": 1, "hx_selected_attention": 1}
+            "hx_quest_compact": 1, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_merge_partials": 1,
+            "hx_selected_attention": 1}
 launch_count = [0]
 
 
@@ -107,7 +111,8 @@ def call(name, *args):
     rc = getattr(lib(), name)(*args)
     if rc != HX_OK:
         what = {HX_ERR_ARG: "invalid argument", HX_ERR_UNSUPPORTED: "unsupported configuration",
-                HX_ERR_LAUNCH: "CUDA launch failed"}.get(rc, f"status {rc}")
+                HX_ERR_LAUNCH: "CUDA launch failed",
+                HX_ERR_SCRATCH_LIMIT: "request exceeds the fixed scratch size"}.get(rc, f"status {rc}")
         raise HelixError(f"{name}: {what}")
     return rc
 

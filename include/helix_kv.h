@@ -42,6 +42,7 @@ extern "C" {
 #define HX_ERR_ARG         1   /* shape, pointer or size rejected */
 #define HX_ERR_UNSUPPORTED 2   /* valid request this build has no kernel for */
 #define HX_ERR_LAUNCH      3   /* the CUDA launch itself failed */
+#define HX_ERR_SCRATCH_LIMIT 4 /* request exceeds a fixed scratch array's size */
 
 /* device error bits, OR-ed into *dev_err */
 #define HX_DEV_ERR_ARENA_FULL 0x1u  /* outlier arena exhausted: entries dropped */
@@ -239,6 +240,31 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
                           const int32_t* lists, int32_t list_stride, const int32_t* list_counts,
                           int32_t n_splits, void* scratch, float* o, float* lse, uint16_t* out16,
                           uint32_t* dev_err);
+
+/*
+ * hx_decode_attn without a caller scratch buffer: no counterpart in the
+ * reference. Its scratch is a fixed array inside this library (64 KB of split
+ * counters + 1024 split partials, about 4.3 MB per GPU that loads the
+ * library, held until exit), so the call allocates nothing and needs nothing
+ * allocated for it. Meant for callers that cannot call cudaMalloc: a serving
+ * engine that has reserved nearly all HBM for its own KV pool and forbids
+ * allocation during decode, or a foreign-language binding that holds raw
+ * device pointers but no allocator. B * H * n_splits must be <= 1024, else
+ * HX_ERR_SCRATCH_LIMIT and nothing runs. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture. Each call clears the
+ * counters it needs (a memset on `stream`) because the array keeps the last
+ * call's contents. All calls share the one array: calls that overlap on the
+ * GPU (other streams, other threads) race and must be serialised by the caller.
+ */
+HX_API int hx_decode_attn_noalloc(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
+                                  const uint16_t* q, int32_t B, int32_t group, float softmax_scale,
+                                  const int32_t* block_table, int32_t bt_stride, const int32_t* seq_lens,
+                                  int32_t page_begin, int32_t max_pages, int32_t sel_mode,
+                                  const float* scores, const uint64_t* thresh, int32_t sink_pages,
+                                  const int32_t* lists, int32_t list_stride, const int32_t* list_counts,
+                                  int32_t n_splits, float* o, float* lse, uint16_t* out16,
+                                  uint32_t* dev_err);
 
 /* Merge R shards' (o, lse): o_parts (R, N, D) fp32, lse_parts (R, N) ->
  * o (N, D) fp32, lse (N), out16 (N, D) fp16 if non-NULL. Used after the
