@@ -133,7 +133,104 @@ __global__ void __launch_bounds__(256) quest_scores_kernel(const uint16_t* __res
     for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
     if (lane == 0) {
       scores[(int64_t)bh * max_pages + j] = acc;
-      if (hist && j >= sinks) atomicAdd(&hist[(int64_t)bh * kBins + (order_key(acc) >> 20)], 1u);
+      if (hist && j >= sinks) atomicAdd(&hist[(int64_t)bh * 2 * kBins + (order_key(acc) >> 20)], 1u);
+    }
+  }
+}
+
+// Fast path for fp16 stats with D = 128 (4 channels per lane): a warp scores
+// 32 consecutive pages at once. Lane partials follow the pinned order; the
+// 32 per-page butterflies are done as one transposed butterfly (stage m adds
+// the same lane pairs l, l ^ m as the per-page butterfly, so every page's sum
+// is the same tree and bit-identical), after which lane l holds page base + l.
+__global__ void __launch_bounds__(256) quest_scores_d128_kernel(const uint16_t* __restrict__ q, int H, int G,
+                                                                int mode, const uint16_t* __restrict__ kmin,
+                                                                const uint16_t* __restrict__ kmax,
+                                                                int64_t page_stride, int64_t head_stride,
+                                                                const int32_t* __restrict__ bt, int bt_stride,
+                                                                const int32_t* __restrict__ seq_lens, int S,
+                                                                int max_pages, int sinks_req,
+                                                                float* __restrict__ scores,
+                                                                uint32_t* __restrict__ hist) {
+  __shared__ float s_qp[128], s_qn[128];
+  __shared__ uint32_t s_hist[kBins];  // block-local histogram, flushed once
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  if (threadIdx.x < 128) {
+    float qp, qn;
+    group_terms(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, 128, mode, threadIdx.x, qp, qn);
+    s_qp[threadIdx.x] = qp;
+    s_qn[threadIdx.x] = qn;
+  }
+  if (hist)
+    for (int i = threadIdx.x; i < kBins; i += blockDim.x) s_hist[i] = 0;
+  __syncthreads();
+  const int n = min((seq_lens[b] + S - 1) / S, max_pages);
+  const int sinks = min(max(sinks_req, 0), n);
+  const int lane = lane_id(), warp = threadIdx.x >> 5;
+  const int base = blockIdx.x * 256 + warp * 32;
+  if (base < n) {
+    float qp[4], qn[4];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      qp[v] = s_qp[4 * lane + v];
+      qn[v] = s_qn[4 * lane + v];
+    }
+    float part[32];
+#pragma unroll
+    for (int g8 = 0; g8 < 4; ++g8) {
+      uint2 a[8], c[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = base + 8 * g8 + u;
+        if (j < n) {
+          const int64_t phys = bt ? (int64_t)bt[(int64_t)b * bt_stride + j] : (int64_t)j;
+          const int64_t off = phys * page_stride + (int64_t)h * head_stride + 4 * lane;
+          a[u] = __ldg(reinterpret_cast<const uint2*>(kmax + off));
+          c[u] = __ldg(reinterpret_cast<const uint2*>(kmin + off));
+        } else {
+          a[u] = make_uint2(0u, 0u);
+          c[u] = make_uint2(0u, 0u);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint16_t xa[4] = {(uint16_t)(a[u].x & 0xffff), (uint16_t)(a[u].x >> 16),
+                                (uint16_t)(a[u].y & 0xffff), (uint16_t)(a[u].y >> 16)};
+        const uint16_t xc[4] = {(uint16_t)(c[u].x & 0xffff), (uint16_t)(c[u].x >> 16),
+                                (uint16_t)(c[u].y & 0xffff), (uint16_t)(c[u].y >> 16)};
+        float acc = 0.0f;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          acc = __fadd_rn(acc, __fmul_rn(qp[v], h2f(xa[v])));
+          acc = __fadd_rn(acc, __fmul_rn(qn[v], h2f(xc[v])));
+        }
+        part[8 * g8 + u] = acc;
+      }
+    }
+    // transposed butterfly: stage m adds the pair (l, l ^ m) exactly as the
+    // per-page butterfly does; afterwards lane l holds page base + l
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < m; ++i) {
+        const float send = upper ? part[i] : part[i + m];
+        const float keep = upper ? part[i + m] : part[i];
+        part[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+      }
+    }
+    const int j = base + lane;
+    if (j < n) {
+      scores[(int64_t)bh * max_pages + j] = part[0];
+      if (hist && j >= sinks) atomicAdd(&s_hist[order_key(part[0]) >> 20], 1u);
+    }
+  }
+  if (hist) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
+      const uint32_t c = s_hist[i];
+      if (c) atomicAdd(&hist[(int64_t)bh * 2 * kBins + i], c);
     }
   }
 }
@@ -146,7 +243,8 @@ __global__ void quest_hist_kernel(const float* scores, int H, const int32_t* seq
   const int n = min((seq_lens[b] + S - 1) / S, max_pages);
   const int sinks = min(max(sinks_req, 0), n);
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
-    if (j >= sinks) atomicAdd(&hist[(int64_t)bh * kBins + (order_key(scores[(int64_t)bh * max_pages + j]) >> 20)], 1u);
+    if (j >= sinks)
+      atomicAdd(&hist[(int64_t)bh * 2 * kBins + (order_key(scores[(int64_t)bh * max_pages + j]) >> 20)], 1u);
 }
 
 // ---------------------------------------------------------------------------
@@ -166,135 +264,149 @@ HX_DEVINL SelPlan plan_for(int seq_len, int S, int max_pages, int sinks_req, int
   return p;
 }
 
-// Block-wide: find the highest bin b* whose suffix count reaches `need`.
-// Returns b* and writes the count strictly above it. blockDim == 256.
-HX_DEVINL int find_boundary(const uint32_t* s_hist, uint32_t need, uint32_t& above, int* s_tmp) {
-  // thread t owns bins [16t, 16t+16); suffix sums over threads from the top
-  const int t = threadIdx.x;
-  uint32_t local = 0;
-  for (int i = 0; i < 16; ++i) local += s_hist[16 * t + i];
-  s_tmp[t] = (int)local;
+// Block-wide (256 threads) locate: thread t owns count c_t; with suffix sums
+// S_t = sum_{u >= t} c_u, find the t with S_{t+1} < need <= S_t. Returns t
+// (or -1 if the total is below need) and S_{t+1} in `above`.
+HX_DEVINL int suffix_locate(uint32_t c, uint32_t need, uint32_t& above, uint32_t* s_warp, int* s_res) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  uint32_t v = c;  // inclusive suffix sum within the warp (lanes >= this lane)
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t x = __shfl_down_sync(0xffffffffu, v, o);
+    if (lane + o < 32) v += x;
+  }
+  if (lane == 0) s_warp[w] = v;  // warp total
+  if (t == 0) s_res[0] = -1;
   __syncthreads();
-  if (t == 0) {
-    uint32_t acc = 0;
-    int found = -1;
-    uint32_t above_v = 0;
-    for (int u = 255; u >= 0 && found < 0; --u) {
-      uint32_t c = (uint32_t)s_tmp[u];
-      if (acc + c >= need) {
-        for (int bin = 16 * u + 15; bin >= 16 * u; --bin) {
-          uint32_t hb = s_hist[bin];
-          if (acc + hb >= need) {
-            found = bin;
-            above_v = acc;
-            break;
-          }
-          acc += hb;
-        }
-      } else {
-        acc += c;
-      }
-    }
-    s_tmp[256] = found;
-    s_tmp[257] = (int)above_v;
+  uint32_t later = 0;  // totals of the warps above this one
+  for (int u = w + 1; u < 8; ++u) later += s_warp[u];
+  const uint32_t incl = v + later, excl = incl - c;
+  if (excl < need && incl >= need) {
+    s_res[0] = t;
+    s_res[1] = (int)excl;
   }
   __syncthreads();
-  above = (uint32_t)s_tmp[257];
-  int r = s_tmp[256];
+  const int r = s_res[0];
+  above = r >= 0 ? (uint32_t)s_res[1] : 0u;
   __syncthreads();
   return r;
 }
 
-// Select the r-th largest among `cnt` unique 64-bit keys sharing their top 12
-// bits, by 8-bit digit passes from bit 51 down. Returns the threshold T with
+// Highest histogram bin whose suffix count reaches `need` (4096 bins).
+HX_DEVINL int find_boundary(const uint32_t* s_hist, uint32_t need, uint32_t& above, uint32_t* s_warp,
+                            int* s_res) {
+  const int t = threadIdx.x;
+  uint32_t local = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) local += s_hist[16 * t + i];
+  uint32_t above_t;
+  const int owner = suffix_locate(local, need, above_t, s_warp, s_res);
+  if (owner < 0) return -1;
+  // the owner's 16 bins, scanned from the top by that thread
+  if (t == owner) {
+    uint32_t acc = above_t;
+    int found = 16 * t;
+    for (int bin = 16 * t + 15; bin >= 16 * t; --bin) {
+      if (acc + s_hist[bin] >= need) {
+        found = bin;
+        break;
+      }
+      acc += s_hist[bin];
+    }
+    s_res[2] = found;
+    s_res[3] = (int)acc;
+  }
+  __syncthreads();
+  above = (uint32_t)s_res[3];
+  const int r = s_res[2];
+  __syncthreads();
+  return r;
+}
+
+// Select the r-th largest among `cnt` unique 64-bit keys, counting only keys
+// whose bits above `shift` equal `prefix`, by 8-bit digit passes from bit
+// shift-1 down. Returns the threshold T with
 // exactly r keys >= T (among the candidates). blockDim == 256.
-HX_DEVINL uint64_t radix_select(const uint64_t* cand, uint32_t cnt, uint32_t r, uint64_t prefix, uint32_t* s_h,
-                                int* s_tmp) {
-  uint64_t mask = 0xFFF0000000000000ull;
-  int shift = 52;
+HX_DEVINL uint64_t radix_select(const uint64_t* cand, uint32_t cnt, uint32_t r, uint64_t prefix, int shift,
+                                uint32_t* s_h, uint32_t* s_warp, int* s_res) {
+  uint64_t mask = ~((1ull << shift) - 1ull);
   while (shift > 0) {
-    int width = shift >= 8 ? 8 : shift;
+    const int width = shift >= 8 ? 8 : shift;
     shift -= width;
     const uint32_t nb = 1u << width;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_h[i] = 0;
+    s_h[threadIdx.x] = 0;
     __syncthreads();
     for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-      uint64_t key = cand[i];
+      const uint64_t key = __ldcg(cand + i);  // written by other blocks
       if ((key & mask) == prefix) atomicAdd(&s_h[(key >> shift) & (nb - 1)], 1u);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t acc = 0;
-      int dsel = 0;
-      for (int dg = (int)nb - 1; dg >= 0; --dg) {
-        if (acc + s_h[dg] >= r) {
-          dsel = dg;
-          break;
-        }
-        acc += s_h[dg];
-      }
-      s_tmp[0] = dsel;
-      s_tmp[1] = (int)acc;
-      s_tmp[2] = (int)s_h[dsel];
-    }
+    uint32_t above;
+    const int dsel = suffix_locate(threadIdx.x < nb ? s_h[threadIdx.x] : 0u, r, above, s_warp, s_res);
+    const uint32_t in_bin = dsel >= 0 ? s_h[dsel] : 0u;
     __syncthreads();
-    const uint64_t dsel = (uint64_t)s_tmp[0];
-    r -= (uint32_t)s_tmp[1];
-    const uint32_t in_bin = (uint32_t)s_tmp[2];
-    __syncthreads();
-    prefix |= dsel << shift;
+    if (dsel < 0) return prefix;  // inconsistent counts; the caller flags it
+    r -= above;
+    prefix |= (uint64_t)dsel << shift;
     mask |= (uint64_t)(nb - 1) << shift;
     if (in_bin == r) return prefix;  // every key with this prefix is selected
   }
   return prefix;
 }
 
+// hist layout per (b, h): [level 1: 4096 bins of key32 >> 20 | level 2: 4096
+// bins of key32 bits 19..8 among the level-1 boundary bin's pages].
 __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __restrict__ scores, int H,
                                                               const int32_t* __restrict__ seq_lens, int S,
                                                               int max_pages, int sinks_req, int k_fixed, int fnum,
                                                               int fden, uint32_t* hist, uint64_t* cand,
                                                               uint32_t* counters, uint64_t* thresh, uint32_t* err) {
   __shared__ uint32_t s_hist[kBins];
-  __shared__ int s_tmp[260];
+  __shared__ uint32_t s_warp[8];
+  __shared__ int s_res[4];
   __shared__ uint32_t s_h2[256];
   __shared__ int s_last;
   const int bh = blockIdx.y;
   const int b = bh / H;
   const int C = gridDim.x;
   const SelPlan pl = plan_for(seq_lens[b], S, max_pages, sinks_req, k_fixed, fnum, fden);
-  uint32_t* hist_bh = hist + (int64_t)bh * kBins;
+  uint32_t* hist_bh = hist + (int64_t)bh * 2 * kBins;
+  uint32_t* hist2_bh = hist_bh + kBins;
   uint32_t* ctr = counters + 2 * (int64_t)bh;
   uint64_t* cand_bh = cand + (int64_t)bh * max_pages;
   const int n_ns = pl.n - pl.sinks;
 
   int bstar = -1;
   uint32_t above = 0, r = 0;
+  bool full_bin = false;
   const bool trivial = (pl.k_eff == 0) || (pl.k_eff >= n_ns);
   if (!trivial) {
     for (int i = threadIdx.x; i < kBins; i += blockDim.x) s_hist[i] = hist_bh[i];
     __syncthreads();
-    bstar = find_boundary(s_hist, (uint32_t)pl.k_eff, above, s_tmp);
+    bstar = find_boundary(s_hist, (uint32_t)pl.k_eff, above, s_warp, s_res);
     r = (uint32_t)pl.k_eff - above;
-    const bool full_bin = bstar >= 0 && s_hist[bstar] == r;
+    full_bin = bstar >= 0 && s_hist[bstar] == r;
     if (bstar >= 0 && !full_bin) {
-      // collect this block's candidates of bin b*
+      // this block's candidates of bin b*, with their level-2 histogram
       const int per = (n_ns + C - 1) / C;
       const int a = pl.sinks + blockIdx.x * per;
       const int e = min(a + per, pl.n);
       for (int base = a; base < e; base += blockDim.x) {
-        int j = base + threadIdx.x;
+        const int j = base + threadIdx.x;
         bool hit = false;
-        uint64_t key = 0;
+        uint32_t k32 = 0;
         if (j < e) {
-          float s = scores[(int64_t)bh * max_pages + j];
-          hit = (int)(order_key(s) >> 20) == bstar;
-          key = order_key64(s, (uint32_t)j);
+          k32 = order_key(scores[(int64_t)bh * max_pages + j]);
+          hit = (int)(k32 >> 20) == bstar;
         }
-        uint32_t m = __ballot_sync(0xffffffffu, hit);
+        const uint32_t m = __ballot_sync(0xffffffffu, hit);
         uint32_t pos = 0;
         if (lane_id() == 0 && m) pos = atomicAdd(&ctr[0], (uint32_t)__popc(m));
         pos = __shfl_sync(0xffffffffu, pos, 0);
-        if (hit) cand_bh[pos + __popc(m & ((1u << lane_id()) - 1))] = key;
+        if (hit) {
+          cand_bh[pos + __popc(m & ((1u << lane_id()) - 1))] = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
+          atomicAdd(&hist2_bh[(k32 >> 8) & (kBins - 1)], 1u);
+        }
       }
     }
   }
@@ -313,19 +425,30 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
   } else if (bstar < 0) {
     T = 0ull;
     if (threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
-  } else if (s_hist[bstar] == r) {
+  } else if (full_bin) {
     T = (uint64_t)bstar << 52;
   } else {
     const uint32_t cnt = *((volatile uint32_t*)&ctr[0]);
-    if (cnt != s_hist[bstar] && threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
-    T = radix_select(cand_bh, cnt, r, (uint64_t)bstar << 52, s_h2, s_tmp);
+    for (int i = threadIdx.x; i < kBins; i += blockDim.x) s_hist[i] = __ldcg(&hist2_bh[i]);
+    __syncthreads();
+    uint32_t above2;
+    const int b2 = find_boundary(s_hist, r, above2, s_warp, s_res);
+    if (b2 < 0) {
+      T = (uint64_t)bstar << 52;
+      if (threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
+    } else {
+      const uint32_t r2 = r - above2;
+      const uint64_t pre = ((uint64_t)bstar << 52) | ((uint64_t)b2 << 40);
+      if (s_hist[b2] == r2) T = pre;
+      else T = radix_select(cand_bh, cnt, r2, pre, 40, s_h2, s_warp, s_res);
+    }
   }
   if (threadIdx.x == 0) {
     thresh[bh] = T;
     ctr[0] = 0;
     ctr[1] = 0;
   }
-  for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist_bh[i] = 0;
+  for (int i = threadIdx.x; i < 2 * kBins; i += blockDim.x) hist_bh[i] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -431,6 +554,14 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
                                                     page_stride, head_stride, block_table, bt_stride, seq_lens,    \
                                                     page_size, max_pages, sink_pages, ppb, scores, hist)
   bool aligned = (((uintptr_t)kmin | (uintptr_t)kmax) & 7) == 0 && page_stride % 4 == 0 && head_stride % 4 == 0;
+  if (stats_dtype == 1 && D == 128 && aligned) {
+    dim3 g2((max_pages + 255) / 256, B * H);
+    quest_scores_d128_kernel<<<g2, 256, 0, s>>>(q, H, group, gqa_mode, (const uint16_t*)kmin, (const uint16_t*)kmax,
+                                                page_stride, head_stride, block_table, bt_stride, seq_lens, page_size,
+                                                max_pages, sink_pages, scores, hist);
+    HX_LAUNCH_CHECK();
+    return HX_OK;
+  }
   if (stats_dtype == 1) {
     if (V == 4 && D == 128 && !aligned) return HX_ERR_ARG;
     if (V == 1) HX_SC(uint16_t, 1);

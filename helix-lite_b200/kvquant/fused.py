@@ -73,7 +73,7 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
         scores = torch.empty((B, H, max(mp, 1)), dtype=torch.float32, device=dev)
     if thresh is None:
         thresh = torch.empty((B * H,), dtype=torch.int64, device=dev)
-    hist = hxlib.scratch(dev, "quest_hist", B * H * 4096 * 4)
+    hist = hxlib.scratch(dev, "quest_hist", B * H * 2 * 4096 * 4)
     cand = hxlib.scratch(dev, "quest_cand", B * H * max(mp, 1) * 8)
     ctr = hxlib.scratch(dev, "quest_ctr", B * H * 2 * 4)
     stats = lay.stats

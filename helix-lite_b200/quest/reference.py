@@ -114,7 +114,7 @@ def topk_pages_with_sinks(bound: torch.Tensor, k: int, sink_pages: int = 1) -> t
     scores = bound.float().t().contiguous().reshape(1, H, P)
     sl = torch.tensor([P], dtype=torch.int32, device=dev)
     thresh = torch.empty((H,), dtype=torch.int64, device=dev)
-    hist = hxlib.scratch(dev, "quest_hist", H * 4096 * 4)
+    hist = hxlib.scratch(dev, "quest_hist", H * 2 * 4096 * 4)
     cand = hxlib.scratch(dev, "quest_cand", H * P * 8)
     ctr = hxlib.scratch(dev, "quest_ctr", H * 2 * 4)
     n_out = sinks + k_eff

@@ -170,8 +170,9 @@ HX_API int hx_page_stats(void* stream, int32_t dtype, const void* k_pages,
  *   block_table ? block_table[b*bt_stride + j] : j,
  * with dtype 0 fp32 / 1 fp16. q is (B, H*group, D) fp16. Scores (B, H,
  * max_pages) fp32. If hist != NULL, the top 12 bits of each non-sink page's
- * order key are counted into hist (B*H, 4096), which must be zero on entry
- * (hx_quest_threshold leaves it zero again).
+ * order key are counted into hist (B*H, 2, 4096) [level 1; level 2 is used by
+ * hx_quest_threshold], which must be zero on entry (hx_quest_threshold
+ * leaves it zero again).
  * Replaces page_upper_bound / page_upper_bound_triton (reference.py:59-93,
  * triton_kernels.py:26-91) and the GQA contraction (compact_backend.py:231).
  */
