@@ -235,6 +235,134 @@ __global__ void __launch_bounds__(256) quest_scores_d128_kernel(const uint16_t* 
   }
 }
 
+// TMA-staged scores for fp16 stats with D = 128 whose min and max rows are
+// adjacent (kmax == kmin + 128, the pool layout). Persistent: each warp takes
+// batches of 32 pages of one (b, h); lane l bulk-copies page l's 512-byte
+// {min, max} record into a 2-stage smem buffer, so 16 KB per warp are in
+// flight; the arithmetic is the pinned order of quest_scores_d128_kernel.
+constexpr int kQW = 4;  // warps per block
+struct __align__(128) QuestSmem {
+  uint16_t rec[kQW][2][32][256];  // [warp][stage][page][min 128 | max 128]
+  uint64_t bar[kQW][2];
+  float qp[kQW][128], qn[kQW][128];
+};
+
+__global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
+    const uint16_t* __restrict__ q, int B, int H, int G, int mode, const uint16_t* __restrict__ kmin,
+    int64_t page_stride, int64_t head_stride, const int32_t* __restrict__ bt, int bt_stride,
+    const int32_t* __restrict__ seq_lens, int S, int max_pages, int sinks_req, float* __restrict__ scores,
+    uint32_t* __restrict__ hist, uint32_t* err) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  QuestSmem& sm = *reinterpret_cast<QuestSmem*>(smem_raw);
+  const int lane = lane_id(), warp = threadIdx.x >> 5;
+  const int nb = (max_pages + 31) / 32;               // batches per (b, h)
+  const int64_t total = (int64_t)B * H * nb;
+  const int64_t gw = (int64_t)blockIdx.x * kQW + warp, nw = (int64_t)gridDim.x * kQW;
+  if (lane == 0) {
+    mbar_init(&sm.bar[warp][0], 1);
+    mbar_init(&sm.bar[warp][1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int cur_bh = -1;  // the (b, h) whose histogram bins this block holds
+  uint32_t phase = 0;
+  bool dead = false;
+
+  // issue the copies of batch `it` (global index) into stage st; returns pages in it
+  auto issue = [&](int64_t it, int st) -> int {
+    const int bh = (int)(it / nb), bi = (int)(it % nb);
+    const int b = bh / H, h = bh % H;
+    const int n = min((seq_lens[b] + S - 1) / S, max_pages);
+    const int j0 = bi * 32;
+    const int cnt = max(0, min(32, n - j0));
+    if (cnt > 0) {
+      if (lane == 0) {
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&sm.bar[warp][st], (uint32_t)cnt * 512u);
+      }
+      __syncwarp();
+      if (lane < cnt) {
+        const int j = j0 + lane;
+        const int64_t phys = bt ? (int64_t)bt[(int64_t)b * bt_stride + j] : (int64_t)j;
+        bulk_g2s(sm.rec[warp][st][lane], kmin + phys * page_stride + (int64_t)h * head_stride, 512u,
+                 &sm.bar[warp][st]);
+      }
+    }
+    return cnt;
+  };
+
+  int64_t it = gw;
+  int cnt_cur = it < total ? issue(it, 0) : 0;
+  int k = 0;
+  for (; it < total; it += nw, ++k) {
+    const int st = k & 1;
+    const int64_t nxt = it + nw;
+    const int cnt_nxt = nxt < total ? issue(nxt, st ^ 1) : 0;
+    const int bh = (int)(it / nb), bi = (int)(it % nb);
+    const int b = bh / H, h = bh % H;
+    const int n = min((seq_lens[b] + S - 1) / S, max_pages);
+    const int sinks = min(max(sinks_req, 0), n);
+    if (cnt_cur > 0) {
+      if (!dead && !mbar_wait(&sm.bar[warp][st], (phase >> st) & 1u)) {
+        dead = true;
+        if (lane == 0) set_err(err, HX_DEV_ERR_TIMEOUT);
+      }
+      phase ^= 1u << st;
+      // group terms of this (b, h), cached per warp
+      if (bh != cur_bh) {
+        for (int d = lane; d < 128; d += 32) {
+          float qp, qn;
+          group_terms(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, 128, mode, d, qp, qn);
+          sm.qp[warp][d] = qp;
+          sm.qn[warp][d] = qn;
+        }
+        __syncwarp();
+      }
+      float qp[4], qn[4];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        qp[v] = sm.qp[warp][4 * lane + v];
+        qn[v] = sm.qn[warp][4 * lane + v];
+      }
+      float part[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const uint2 c = *reinterpret_cast<const uint2*>(&sm.rec[warp][st][u][4 * lane]);
+        const uint2 a = *reinterpret_cast<const uint2*>(&sm.rec[warp][st][u][128 + 4 * lane]);
+        const uint16_t xa[4] = {(uint16_t)(a.x & 0xffff), (uint16_t)(a.x >> 16), (uint16_t)(a.y & 0xffff),
+                                (uint16_t)(a.y >> 16)};
+        const uint16_t xc[4] = {(uint16_t)(c.x & 0xffff), (uint16_t)(c.x >> 16), (uint16_t)(c.y & 0xffff),
+                                (uint16_t)(c.y >> 16)};
+        float acc = 0.0f;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          acc = __fadd_rn(acc, __fmul_rn(qp[v], h2f(xa[v])));
+          acc = __fadd_rn(acc, __fmul_rn(qn[v], h2f(xc[v])));
+        }
+        part[u] = acc;
+      }
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1) {
+        const bool upper = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < m; ++i) {
+          const float send = upper ? part[i] : part[i + m];
+          const float keep = upper ? part[i + m] : part[i];
+          part[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+        }
+      }
+      const int j = bi * 32 + lane;
+      if (lane < cnt_cur) {
+        scores[(int64_t)bh * max_pages + j] = part[0];
+        if (hist && j >= sinks) atomicAdd(&hist[(int64_t)bh * 2 * kBins + (order_key(part[0]) >> 20)], 1u);
+      }
+      cur_bh = bh;
+    }
+    __syncwarp();
+    cnt_cur = cnt_nxt;
+  }
+}
+
 // Histogram of given scores (for the API path where scores come from outside).
 __global__ void quest_hist_kernel(const float* scores, int H, const int32_t* seq_lens, int S, int max_pages,
                                   int sinks_req, uint32_t* hist) {
@@ -336,9 +464,17 @@ HX_DEVINL uint64_t radix_select(const uint64_t* cand, uint32_t cnt, uint32_t r, 
     const uint32_t nb = 1u << width;
     s_h[threadIdx.x] = 0;
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-      const uint64_t key = __ldcg(cand + i);  // written by other blocks
-      if ((key & mask) == prefix) atomicAdd(&s_h[(key >> shift) & (nb - 1)], 1u);
+    for (uint32_t i0 = 0; i0 < cnt; i0 += 4 * blockDim.x) {
+      uint64_t key[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // written by other blocks: read through L2
+        const uint32_t i = i0 + u * blockDim.x + threadIdx.x;
+        key[u] = i < cnt ? __ldcg(cand + i) : ~prefix;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * blockDim.x + threadIdx.x < cnt && (key[u] & mask) == prefix)
+          atomicAdd(&s_h[(key[u] >> shift) & (nb - 1)], 1u);
     }
     __syncthreads();
     uint32_t above;
@@ -391,21 +527,30 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
       const int per = (n_ns + C - 1) / C;
       const int a = pl.sinks + blockIdx.x * per;
       const int e = min(a + per, pl.n);
-      for (int base = a; base < e; base += blockDim.x) {
-        const int j = base + threadIdx.x;
-        bool hit = false;
-        uint32_t k32 = 0;
-        if (j < e) {
-          k32 = order_key(scores[(int64_t)bh * max_pages + j]);
-          hit = (int)(k32 >> 20) == bstar;
+      for (int base = a; base < e; base += 4 * blockDim.x) {
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {  // loads first, so they are in flight together
+          const int j = base + u * blockDim.x + threadIdx.x;
+          v[u] = j < e ? scores[(int64_t)bh * max_pages + j] : 0.0f;
         }
-        const uint32_t m = __ballot_sync(0xffffffffu, hit);
-        uint32_t pos = 0;
-        if (lane_id() == 0 && m) pos = atomicAdd(&ctr[0], (uint32_t)__popc(m));
-        pos = __shfl_sync(0xffffffffu, pos, 0);
-        if (hit) {
-          cand_bh[pos + __popc(m & ((1u << lane_id()) - 1))] = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
-          atomicAdd(&hist2_bh[(k32 >> 8) & (kBins - 1)], 1u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = base + u * blockDim.x + threadIdx.x;
+          bool hit = false;
+          uint32_t k32 = 0;
+          if (j < e) {
+            k32 = order_key(v[u]);
+            hit = (int)(k32 >> 20) == bstar;
+          }
+          const uint32_t m = __ballot_sync(0xffffffffu, hit);
+          uint32_t pos = 0;
+          if (lane_id() == 0 && m) pos = atomicAdd(&ctr[0], (uint32_t)__popc(m));
+          pos = __shfl_sync(0xffffffffu, pos, 0);
+          if (hit) {
+            cand_bh[pos + __popc(m & ((1u << lane_id()) - 1))] = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
+            atomicAdd(&hist2_bh[(k32 >> 8) & (kBins - 1)], 1u);
+          }
         }
       }
     }
@@ -554,6 +699,26 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
                                                     page_stride, head_stride, block_table, bt_stride, seq_lens,    \
                                                     page_size, max_pages, sink_pages, ppb, scores, hist)
   bool aligned = (((uintptr_t)kmin | (uintptr_t)kmax) & 7) == 0 && page_stride % 4 == 0 && head_stride % 4 == 0;
+  if (stats_dtype == 1 && D == 128 && aligned && head_stride % 8 == 0 && page_stride % 8 == 0 &&
+      ((uintptr_t)kmin & 15) == 0 && (const uint16_t*)kmax == (const uint16_t*)kmin + 128) {
+    static bool attr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_ERR_LAUNCH;
+    if (!attr[dev]) {
+      if (cudaFuncSetAttribute(quest_scores_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)sizeof(QuestSmem)) != cudaSuccess)
+        return HX_ERR_LAUNCH;
+      attr[dev] = true;
+    }
+    int64_t batches = (int64_t)B * H * ((max_pages + 31) / 32);
+    int64_t want = (batches + kQW - 1) / kQW;
+    int grid = (int)(want < 148 ? want : 148);
+    quest_scores_tma_kernel<<<grid, kQW * 32, sizeof(QuestSmem), s>>>(
+        q, B, H, group, gqa_mode, (const uint16_t*)kmin, page_stride, head_stride, block_table, bt_stride,
+        seq_lens, page_size, max_pages, sink_pages, scores, hist, nullptr);
+    HX_LAUNCH_CHECK();
+    return HX_OK;
+  }
   if (stats_dtype == 1 && D == 128 && aligned) {
     dim3 g2((max_pages + 255) / 256, B * H);
     quest_scores_d128_kernel<<<g2, 256, 0, s>>>(q, H, group, gqa_mode, (const uint16_t*)kmin, (const uint16_t*)kmax,
@@ -592,8 +757,8 @@ HX_API int hx_quest_threshold(void* stream, const float* scores, int32_t B, int3
     if (hg.x == 0) hg.x = 1;
     quest_hist_kernel<<<hg, 256, 0, st>>>(scores, H, seq_lens, page_size, max_pages, sink_pages, hist);
   }
-  int C = (max_pages + 4095) / 4096;
-  C = C < 1 ? 1 : (C > 64 ? 64 : C);
+  int C = (max_pages + 1023) / 1024;
+  C = C < 1 ? 1 : (C > 128 ? 128 : C);
   dim3 grid(C, B * H);
   quest_threshold_kernel<<<grid, 256, 0, st>>>(scores, H, seq_lens, page_size, max_pages, sink_pages,
                                                        k_fixed, frac_num, frac_den, hist, cand, counters, thresh,
