@@ -19,13 +19,16 @@
 
 namespace hx {
 
-constexpr int DD = 128;        // head_size
-constexpr int DS = 16;         // page size (tokens)
-constexpr int NW = 4;          // warps per CTA
-constexpr int LISTCAP = 512;   // pages gathered per round
-constexpr int ENTCAP = 128;    // outlier entries staged per page per K|V
+constexpr int DD = 128;          // head_size
+constexpr int DS = 16;           // page size (tokens)
+constexpr int NW = 12;           // warps per CTA (one CTA per SM)
+constexpr int NT = NW * 32;
+constexpr int NSTAGE = 3;        // pages in smem per warp (two in flight while one is used)
+constexpr int LISTCAP = 256;     // pages gathered per round
+constexpr int ENTCAP = 128;      // outlier entries staged per page per K|V
 constexpr int SEGMAX = DS * DD;  // codes bytes per page segment at 4+4 bits
-constexpr int PSZ = 8 * DD + 16;  // floats per split partial: O[8][128], m[8], l[8]
+constexpr int PSZ = 8 * DD + 16; // floats per split partial: O[8][128], m[8], l[8]
+constexpr int MAXSPLIT = 1024;   // splits the final merge stages weights for
 
 struct DecodeParams {
   hx_pool_layer pool;
@@ -53,19 +56,21 @@ struct DecodeParams {
 };
 
 struct __align__(128) WarpSmem {
-  uint8_t raw[2][SEGMAX];            // code segments, 2 stages
-  uint32_t ent[2][2][ENTCAP];        // [stage][K|V] outlier entries
-  uint16_t tile[DS * DD];            // dequantised K, then V (swizzled rows)
-  uint16_t vlut[DS * 16];            // per-token V levels of the current page
-  uint64_t bar[2];
+  uint8_t raw[NSTAGE][SEGMAX];          // code segments
+  uint32_t ent[NSTAGE][2][ENTCAP];      // [stage][K|V] outlier entries
+  uint16_t tile[DS * DD];               // dequantised K, then V (swizzled rows)
+  uint16_t vlut[DS * 16];               // per-token V levels of the current page
+  uint64_t bar[NSTAGE];
 };
 
 struct __align__(128) CtaSmem {
   WarpSmem w[NW];
-  uint16_t klut[16 * DD + 64];       // per-channel K levels (bank-spread)
-  uint16_t vtail[16];                // V levels at positions >= t_cal
+  uint16_t klut[16 * DD + 64];          // per-channel K levels (bank-spread)
+  uint16_t vtail[16];                   // V levels at positions >= t_cal
   int32_t pages[LISTCAP];
   int32_t phys[LISTCAP];
+  uint4 dir[LISTCAP][2];                // K and V directory records of each page
+  float colM[8], colL[8];               // per-column max / sum for the merges
   int32_t count;
   int32_t wcount[NW];
   int32_t last;
@@ -76,7 +81,7 @@ struct __align__(128) CtaSmem {
 HX_DEVINL int tile_off(int t, int d) { return t * DD + ((((d >> 3) ^ (t & 7))) << 3) + (d & 7); }
 
 template <int BK, int BV>
-__global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   CtaSmem& sm = *reinterpret_cast<CtaSmem*>(smem_raw);
   constexpr int NLK = 1 << BK, NLV = 1 << BV;
@@ -94,7 +99,7 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
   const int n = min((seq_len + DS - 1) / DS, p.max_pages);
 
   // ---- per-CTA tables
-  for (int i = tid; i < NLK * DD; i += blockDim.x) {
+  for (int i = tid; i < NLK * DD; i += NT) {
     int d = i / NLK, c = i % NLK;
     sm.klut[NLK * d + 32 * (d >> 6) + c] =
         c < p.sc.levels_k ? p.sc.k_poles[((int64_t)h * DD + d) * p.sc.levels_k + c] : (uint16_t)0;
@@ -103,8 +108,7 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
     sm.vtail[tid] = tid < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + (Tc - 1)) * p.sc.levels_v + tid] : (uint16_t)0;
   WarpSmem& ws = sm.w[warp];
   if (lane == 0) {
-    mbar_init(&ws.bar[0], 1);
-    mbar_init(&ws.bar[1], 1);
+    for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
     fence_mbar_init();
   }
 
@@ -148,8 +152,8 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
     const int rend = min(rb + LISTCAP, re);
     if (tid == 0) sm.count = 0;
     __syncthreads();
-    // gather the round's selected pages in ascending order
-    for (int base = rb; base < rend; base += blockDim.x) {
+    // gather the round's selected pages (ascending) with their directory records
+    for (int base = rb; base < rend; base += NT) {
       int idx = base + tid;
       int j = -1;
       bool sel = false;
@@ -171,6 +175,12 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
           sel = false;
         }
       }
+      uint4 d0 = make_uint4(0, 0, 0, 0), d1 = d0;
+      if (sel) {
+        const uint4* dr = reinterpret_cast<const uint4*>(p.pool.dir + ((int64_t)h * NB + pp) * 8);
+        d0 = dr[0];
+        d1 = dr[1];
+      }
       uint32_t m = __ballot_sync(0xffffffffu, sel);
       if (lane == 0) sm.wcount[warp] = __popc(m);
       __syncthreads();
@@ -180,6 +190,8 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
         int pos = off + __popc(m & ((1u << lane) - 1));
         sm.pages[pos] = j;
         sm.phys[pos] = pp;
+        sm.dir[pos][0] = d0;
+        sm.dir[pos][1] = d1;
       }
       __syncthreads();
       if (tid == 0) {
@@ -193,41 +205,28 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
     const int my_n = cnt > warp ? (cnt - warp + NW - 1) / NW : 0;
 
     // ---- warp pipeline over pages warp, warp + NW, ...
-    auto dir_word = [&](int k) -> uint32_t {
-      // lanes 0-7 read the K and V directory records of the k-th page
-      if (lane < 8) {
-        int pp = sm.phys[warp + NW * k];
-        return p.pool.dir[((int64_t)h * NB + pp) * 8 + lane];
-      }
-      return 0u;
-    };
-    auto issue = [&](int k, uint32_t dw) {
+    auto issue = [&](int k) {
       if (timed_out) return;
-      inflight |= 1u << (k & 1);
-      const uint32_t offk = __shfl_sync(0xffffffffu, dw, 0), cntk = __shfl_sync(0xffffffffu, dw, 2);
-      const uint32_t offv = __shfl_sync(0xffffffffu, dw, 4), cntv = __shfl_sync(0xffffffffu, dw, 6);
+      const int st = k % NSTAGE;
+      inflight |= 1u << st;
       if (lane == 0) {
-        const int st = k & 1;
-        const int pp = sm.phys[warp + NW * k];
-        const uint32_t ek = min((cntk + 3u) & ~3u, (uint32_t)ENTCAP);
-        const uint32_t ev = min((cntv + 3u) & ~3u, (uint32_t)ENTCAP);
+        const int li = warp + NW * k;
+        const int pp = sm.phys[li];
+        const uint4 dk = sm.dir[li][0], dv = sm.dir[li][1];
+        const uint32_t ek = min((dk.z + 3u) & ~3u, (uint32_t)ENTCAP);
+        const uint32_t ev = min((dv.z + 3u) & ~3u, (uint32_t)ENTCAP);
         fence_proxy_async();
         mbar_arrive_expect_tx(&ws.bar[st], SEG + 4u * (ek + ev));
         bulk_g2s(ws.raw[st], p.pool.codes + ((int64_t)h * NB + pp) * SEG, SEG, &ws.bar[st]);
-        if (ek) bulk_g2s(ws.ent[st][0], p.pool.arena + offk, 4u * ek, &ws.bar[st]);
-        if (ev) bulk_g2s(ws.ent[st][1], p.pool.arena + offv, 4u * ev, &ws.bar[st]);
+        if (ek) bulk_g2s(ws.ent[st][0], p.pool.arena + dk.x, 4u * ek, &ws.bar[st]);
+        if (ev) bulk_g2s(ws.ent[st][1], p.pool.arena + dv.x, 4u * ev, &ws.bar[st]);
       }
     };
 
-    uint32_t dcur = 0, dn1 = 0;
-    if (my_n > 0) dcur = dir_word(0);
-    if (my_n > 1) dn1 = dir_word(1);
-    if (my_n > 0) issue(0, dcur);
-
+    for (int k = 0; k < NSTAGE - 1 && k < my_n; ++k) issue(k);
     for (int k = 0; k < my_n; ++k) {
-      const int st = k & 1;
-      if (k + 1 < my_n) issue(k + 1, dn1);
-      uint32_t dn2 = (k + 2 < my_n) ? dir_word(k + 2) : 0u;
+      const int st = k % NSTAGE;
+      if (k + NSTAGE - 1 < my_n) issue(k + NSTAGE - 1);  // its stage held page k - 1, done
       if (!timed_out) {
         if (mbar_wait(&ws.bar[st], (phase >> st) & 1u)) {
           phase ^= 1u << st;
@@ -237,14 +236,11 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
           if (lane == 0) set_err(p.err, HX_DEV_ERR_TIMEOUT);
         }
       }
-      if (timed_out) {
-        dcur = dn1;
-        dn1 = dn2;
-        continue;
-      }
-      const uint32_t offk = __shfl_sync(0xffffffffu, dcur, 0), cntk = __shfl_sync(0xffffffffu, dcur, 2);
-      const uint32_t offv = __shfl_sync(0xffffffffu, dcur, 4), cntv = __shfl_sync(0xffffffffu, dcur, 6);
-      const int j = sm.pages[warp + NW * k];
+      if (timed_out) continue;
+      const int li = warp + NW * k;
+      const uint4 dk = sm.dir[li][0], dv = sm.dir[li][1];
+      const uint32_t offk = dk.x, cntk = dk.z, offv = dv.x, cntv = dv.z;
+      const int j = sm.pages[li];
       const int pos0 = (p.page_begin + j) * DS;
       const int valid = seq_len - j * DS;  // tokens of this page inside the sequence
 
@@ -295,19 +291,20 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
       }
       __syncwarp();
 
-      // ---- S^T = K . Q^T  (16 tokens x 8 head columns)
-      float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // ---- S^T = K . Q^T  (16 tokens x 8 head columns), two accumulator chains
+      float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         uint32_t a[4];
         const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
         const int chunk = (2 * ks + (lane >> 4)) ^ (r & 7);
         ldmatrix_x4(a, ws.tile + r * DD + chunk * 8);
-        mma_16816(sacc, a, bq[ks][0], bq[ks][1]);
+        if (ks & 1) mma_16816(sb, a, bq[ks][0], bq[ks][1]);
+        else mma_16816(sa, a, bq[ks][0], bq[ks][1]);
       }
       // ---- online softmax (exp2 domain); rows = tokens g, g+8; cols = 2qd, 2qd+1
-      float x0 = sacc[0] * p.scale_log2, x1 = sacc[1] * p.scale_log2;
-      float x2 = sacc[2] * p.scale_log2, x3 = sacc[3] * p.scale_log2;
+      float x0 = (sa[0] + sb[0]) * p.scale_log2, x1 = (sa[1] + sb[1]) * p.scale_log2;
+      float x2 = (sa[2] + sb[2]) * p.scale_log2, x3 = (sa[3] + sb[3]) * p.scale_log2;
       if (g >= valid) x0 = x1 = -INFINITY;
       if (g + 8 >= valid) x2 = x3 = -INFINITY;
       float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
@@ -409,13 +406,11 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
         mma_16816(oacc[mt], a, bl0, bl1);
       }
       __syncwarp();
-      dcur = dn1;
-      dn1 = dn2;
     }
     if (timed_out) {
       // give copies still in flight one more bounded wait before the buffers
       // are reused, then stop this warp's work
-      for (int st = 0; st < 2; ++st)
+      for (int st = 0; st < NSTAGE; ++st)
         if ((inflight >> st) & 1u && mbar_wait(&ws.bar[st], (phase >> st) & 1u)) {
           phase ^= 1u << st;
           inflight &= ~(1u << st);
@@ -448,26 +443,36 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
     wml[8 + 2 * qd + 1] = l1;
   }
   __syncthreads();
-  float* mypart = p.part + ((int64_t)bh * p.n_splits + split) * PSZ;
-  {
-    const int d = tid;  // 128 threads = 128 channels
-    for (int c = 0; c < G; ++c) {
-      float M = -INFINITY;
-      for (int w = 0; w < NW; ++w) M = fmaxf(M, reinterpret_cast<float*>(sm.w[w].vlut)[c]);
-      const float base = M == -INFINITY ? 0.0f : M;
-      float L = 0.0f, O = 0.0f;
-      for (int w = 0; w < NW; ++w) {
-        const float* ml = reinterpret_cast<float*>(sm.w[w].vlut);
-        const float sc = exp2f(ml[c] - base);
-        L += sc * ml[8 + c];
-        O += sc * reinterpret_cast<float*>(sm.w[w].raw)[c * DD + d];
-      }
-      mypart[c * DD + d] = O;
-      if (d == 0) {
-        mypart[8 * DD + c] = M;
-        mypart[8 * DD + 8 + c] = L;
-      }
+  // per-column warp maxima and sums, then (column, channel) sums over the warps
+  if (tid < G) {
+    const int c = tid;
+    float M = -INFINITY;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, reinterpret_cast<float*>(sm.w[w].vlut)[c]);
+    const float base = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f;
+    for (int w = 0; w < NW; ++w) {
+      const float* ml = reinterpret_cast<float*>(sm.w[w].vlut);
+      L += exp2f(ml[c] - base) * ml[8 + c];
     }
+    sm.colM[c] = M;
+    sm.colL[c] = L;
+  }
+  __syncthreads();
+  float* mypart = p.part + ((int64_t)bh * p.n_splits + split) * PSZ;
+  for (int i = tid; i < G * DD; i += NT) {
+    const int c = i / DD, d = i % DD;
+    const float M = sm.colM[c];
+    const float base = M == -INFINITY ? 0.0f : M;
+    float O = 0.0f;
+    for (int w = 0; w < NW; ++w) {
+      const float sc = exp2f(reinterpret_cast<float*>(sm.w[w].vlut)[c] - base);
+      O += sc * reinterpret_cast<float*>(sm.w[w].raw)[c * DD + d];
+    }
+    mypart[c * DD + d] = O;
+  }
+  if (tid < G) {
+    mypart[8 * DD + tid] = sm.colM[tid];
+    mypart[8 * DD + 8 + tid] = sm.colL[tid];
   }
   __threadfence();
   __syncthreads();
@@ -476,25 +481,47 @@ __global__ void __launch_bounds__(NW * 32) decode_kernel(const DecodeParams p) {
   if (!sm.last) return;
   __threadfence();
 
-  // ---- last CTA of (b, h): merge the splits, normalise, write o / lse
+  // ---- last CTA of (b, h): merge the splits with precomputed weights
+  __syncthreads();  // every thread is past its reads of the warp buffers
   const float* parts = p.part + (int64_t)bh * p.n_splits * PSZ;
-  const int d = tid;
-  for (int c = 0; c < G; ++c) {
+  float* wts = reinterpret_cast<float*>(sm.w);  // [n_splits][8] weights, <= 32 KB of the warp buffers
+  if (tid < G) {
+    const int c = tid;
     float M = -INFINITY;
     for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, __ldcg(parts + (int64_t)s * PSZ + 8 * DD + c));
     const float base = M == -INFINITY ? 0.0f : M;
-    float L = 0.0f, O = 0.0f;
+    float L = 0.0f;
     for (int s = 0; s < p.n_splits; ++s) {
       const float* ps = parts + (int64_t)s * PSZ;
-      const float sc = exp2f(__ldcg(ps + 8 * DD + c) - base);
-      L += sc * __ldcg(ps + 8 * DD + 8 + c);
-      O += sc * __ldcg(ps + c * DD + d);
+      const float w = exp2f(__ldcg(ps + 8 * DD + c) - base);
+      wts[s * 8 + c] = w;
+      L += w * __ldcg(ps + 8 * DD + 8 + c);
     }
+    sm.colM[c] = M;
+    sm.colL[c] = L;
+  }
+  __syncthreads();
+  for (int i = tid; i < G * DD; i += NT) {
+    const int c = i / DD, d = i % DD;
+    const float L = sm.colL[c];
+    float O0 = 0.0f, O1 = 0.0f, O2 = 0.0f, O3 = 0.0f;
+    int s = 0;
+    for (; s + 4 <= p.n_splits; s += 4) {
+      O0 += wts[(s + 0) * 8 + c] * __ldcg(parts + (int64_t)(s + 0) * PSZ + c * DD + d);
+      O1 += wts[(s + 1) * 8 + c] * __ldcg(parts + (int64_t)(s + 1) * PSZ + c * DD + d);
+      O2 += wts[(s + 2) * 8 + c] * __ldcg(parts + (int64_t)(s + 2) * PSZ + c * DD + d);
+      O3 += wts[(s + 3) * 8 + c] * __ldcg(parts + (int64_t)(s + 3) * PSZ + c * DD + d);
+    }
+    for (; s < p.n_splits; ++s) O0 += wts[s * 8 + c] * __ldcg(parts + (int64_t)s * PSZ + c * DD + d);
+    const float O = (O0 + O1) + (O2 + O3);
     const int64_t row = (int64_t)b * H * G + (int64_t)h * G + c;
     const float ov = L > 0.0f ? O / L : 0.0f;
     p.o[row * DD + d] = ov;
     if (p.out16) p.out16[row * DD + d] = f2h(ov);
-    if (d == 0) p.lse[row] = L > 0.0f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+    if (d == 0) {
+      const float M = sm.colM[c];
+      p.lse[row] = L > 0.0f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+    }
   }
   if (tid == 0) p.ctr[bh] = 0;
 }
@@ -618,7 +645,7 @@ static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
     attr_set[dev] = true;
   }
   dim3 grid(p.n_splits, H, p.B);
-  decode_kernel<BK, BV><<<grid, NW * 32, smem, s>>>(p);
+  decode_kernel<BK, BV><<<grid, NT, smem, s>>>(p);
   HX_LAUNCH_CHECK();
   return HX_OK;
 }
@@ -644,7 +671,8 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
                           const int32_t* lists, int32_t list_stride, const int32_t* list_counts, int32_t n_splits,
                           void* scratch, float* o, float* lse, uint16_t* out16, uint32_t* dev_err) {
   if (!pool || !sc || !q || !seq_lens || !o || !lse || !scratch) return HX_ERR_ARG;
-  if (B < 0 || group <= 0 || n_splits <= 0 || max_pages < 0 || page_begin < 0) return HX_ERR_ARG;
+  if (B < 0 || group <= 0 || n_splits <= 0 || n_splits > MAXSPLIT || max_pages < 0 || page_begin < 0)
+    return HX_ERR_ARG;
   if (B == 0) return HX_OK;
   if (pool->head_size != DD || pool->block_size != DS || group > 8) return HX_ERR_UNSUPPORTED;
   if ((pool->bits_k != 2 && pool->bits_k != 4) || (pool->bits_v != 2 && pool->bits_v != 4)) return HX_ERR_ARG;

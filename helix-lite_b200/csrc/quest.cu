@@ -240,10 +240,11 @@ __global__ void __launch_bounds__(256) quest_scores_d128_kernel(const uint16_t* 
 // batches of 32 pages of one (b, h); lane l bulk-copies page l's 512-byte
 // {min, max} record into a 2-stage smem buffer, so 16 KB per warp are in
 // flight; the arithmetic is the pinned order of quest_scores_d128_kernel.
-constexpr int kQW = 4;  // warps per block
+constexpr int kQW = 4;      // warps per block
+constexpr int kQStages = 3; // batches in smem per warp (2 in flight while one is scored)
 struct __align__(128) QuestSmem {
-  uint16_t rec[kQW][2][32][256];  // [warp][stage][page][min 128 | max 128]
-  uint64_t bar[kQW][2];
+  uint16_t rec[kQW][kQStages][32][256];  // [warp][stage][page][min 128 | max 128]
+  uint64_t bar[kQW][kQStages];
   float qp[kQW][128], qn[kQW][128];
 };
 
@@ -255,61 +256,70 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   extern __shared__ __align__(128) uint8_t smem_raw[];
   QuestSmem& sm = *reinterpret_cast<QuestSmem*>(smem_raw);
   const int lane = lane_id(), warp = threadIdx.x >> 5;
-  const int nb = (max_pages + 31) / 32;               // batches per (b, h)
+  const int nb = (max_pages + 31) / 32;  // batches per (b, h)
   const int64_t total = (int64_t)B * H * nb;
   const int64_t gw = (int64_t)blockIdx.x * kQW + warp, nw = (int64_t)gridDim.x * kQW;
   if (lane == 0) {
-    mbar_init(&sm.bar[warp][0], 1);
-    mbar_init(&sm.bar[warp][1], 1);
+    for (int st = 0; st < kQStages; ++st) mbar_init(&sm.bar[warp][st], 1);
     fence_mbar_init();
   }
   __syncthreads();
-  int cur_bh = -1;  // the (b, h) whose histogram bins this block holds
-  uint32_t phase = 0;
-  bool dead = false;
 
-  // issue the copies of batch `it` (global index) into stage st; returns pages in it
-  auto issue = [&](int64_t it, int st) -> int {
-    const int bh = (int)(it / nb), bi = (int)(it % nb);
-    const int b = bh / H, h = bh % H;
+  // Batch k of this warp is global batch gw + k * nw. For a batch: its pages
+  // count (lanes < cnt hold a page) and lane's physical page.
+  struct Bat {
+    int bh, j0, cnt;
+    int64_t phys;
+  };
+  auto plan = [&](int64_t it) -> Bat {
+    Bat r;
+    r.bh = (int)(it / nb);
+    r.j0 = (int)(it % nb) * 32;
+    const int b = r.bh / H;
     const int n = min((seq_lens[b] + S - 1) / S, max_pages);
-    const int j0 = bi * 32;
-    const int cnt = max(0, min(32, n - j0));
-    if (cnt > 0) {
-      if (lane == 0) {
-        fence_proxy_async();
-        mbar_arrive_expect_tx(&sm.bar[warp][st], (uint32_t)cnt * 512u);
-      }
-      __syncwarp();
-      if (lane < cnt) {
-        const int j = j0 + lane;
-        const int64_t phys = bt ? (int64_t)bt[(int64_t)b * bt_stride + j] : (int64_t)j;
-        bulk_g2s(sm.rec[warp][st][lane], kmin + phys * page_stride + (int64_t)h * head_stride, 512u,
-                 &sm.bar[warp][st]);
-      }
+    r.cnt = max(0, min(32, n - r.j0));
+    const int j = r.j0 + lane;
+    r.phys = (lane < r.cnt) ? (bt ? (int64_t)bt[(int64_t)b * bt_stride + j] : (int64_t)j) : 0;
+    return r;
+  };
+  auto issue = [&](const Bat& bb, int st) {
+    if (bb.cnt <= 0) return;
+    if (lane == 0) {
+      fence_proxy_async();
+      mbar_arrive_expect_tx(&sm.bar[warp][st], (uint32_t)bb.cnt * 512u);
     }
-    return cnt;
+    __syncwarp();
+    if (lane < bb.cnt)
+      bulk_g2s(sm.rec[warp][st][lane], kmin + bb.phys * page_stride + (int64_t)(bb.bh % H) * head_stride, 512u,
+               &sm.bar[warp][st]);
   };
 
-  int64_t it = gw;
-  int cnt_cur = it < total ? issue(it, 0) : 0;
-  int k = 0;
-  for (; it < total; it += nw, ++k) {
-    const int st = k & 1;
-    const int64_t nxt = it + nw;
-    const int cnt_nxt = nxt < total ? issue(nxt, st ^ 1) : 0;
-    const int bh = (int)(it / nb), bi = (int)(it % nb);
-    const int b = bh / H, h = bh % H;
-    const int n = min((seq_lens[b] + S - 1) / S, max_pages);
-    const int sinks = min(max(sinks_req, 0), n);
-    if (cnt_cur > 0) {
+  const int nk = gw < total ? (int)((total - 1 - gw) / nw) + 1 : 0;
+  Bat p0 = {0, 0, 0, 0}, p1 = {0, 0, 0, 0}, p2 = {0, 0, 0, 0};
+  if (nk > 0) p0 = plan(gw);
+  if (nk > 1) p1 = plan(gw + nw);
+  if (nk > 2) p2 = plan(gw + 2 * nw);
+  issue(p0, 0);
+  issue(p1, 1 % kQStages);
+  int cur_bh = -1;
+  uint32_t phase = 0;
+  bool dead = false;
+  for (int k = 0; k < nk; ++k) {
+    const int st = k % kQStages;
+    // keep two batches in flight: issue k + 2 now, plan k + 3 (its block-table
+    // reads overlap this batch's work)
+    if (k + 2 < nk) issue(p2, (k + 2) % kQStages);
+    Bat p3 = {0, 0, 0, 0};
+    if (k + 3 < nk) p3 = plan(gw + (int64_t)(k + 3) * nw);
+    const Bat cb = p0;
+    if (cb.cnt > 0) {
       if (!dead && !mbar_wait(&sm.bar[warp][st], (phase >> st) & 1u)) {
         dead = true;
         if (lane == 0) set_err(err, HX_DEV_ERR_TIMEOUT);
       }
       phase ^= 1u << st;
-      // group terms of this (b, h), cached per warp
-      if (bh != cur_bh) {
+      const int b = cb.bh / H, h = cb.bh % H;
+      if (cb.bh != cur_bh) {
         for (int d = lane; d < 128; d += 32) {
           float qp, qn;
           group_terms(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, 128, mode, d, qp, qn);
@@ -317,6 +327,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
           sm.qn[warp][d] = qn;
         }
         __syncwarp();
+        cur_bh = cb.bh;
       }
       float qp[4], qn[4];
 #pragma unroll
@@ -351,15 +362,18 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
           part[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
         }
       }
-      const int j = bi * 32 + lane;
-      if (lane < cnt_cur) {
-        scores[(int64_t)bh * max_pages + j] = part[0];
-        if (hist && j >= sinks) atomicAdd(&hist[(int64_t)bh * 2 * kBins + (order_key(part[0]) >> 20)], 1u);
+      const int j = cb.j0 + lane;
+      if (lane < cb.cnt) {
+        const int n = min((seq_lens[b] + S - 1) / S, max_pages);
+        const int sinks = min(max(sinks_req, 0), n);
+        scores[(int64_t)cb.bh * max_pages + j] = part[0];
+        if (hist && j >= sinks) atomicAdd(&hist[(int64_t)cb.bh * 2 * kBins + (order_key(part[0]) >> 20)], 1u);
       }
-      cur_bh = bh;
     }
     __syncwarp();
-    cnt_cur = cnt_nxt;
+    p0 = p1;
+    p1 = p2;
+    p2 = p3;
   }
 }
 

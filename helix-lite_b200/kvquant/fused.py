@@ -106,8 +106,9 @@ def selected_lists(sel: Selection, union: bool = False, max_out: int | None = No
 
 
 def default_splits(B: int, H: int, max_pages: int) -> int:
-    want = max(1, math.ceil(4 * NUM_SMS / max(1, B * H)))
-    return max(1, min(want, max(1, max_pages // 8)))
+    """Splits per (sequence, head): about one decode CTA (12 warps) per SM."""
+    want = max(1, math.ceil(NUM_SMS / max(1, B * H)))
+    return max(1, min(want, max(1, math.ceil(max_pages / 16))))
 
 
 def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
