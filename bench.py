@@ -232,6 +232,8 @@ def make_step(W, world, group, timing=None):
     dev = pool.device
     scores = [torch.empty((1, H, shard.n_pages), dtype=torch.float32, device=dev) for _ in range(L)]
     thresh = [torch.empty((H,), dtype=torch.int64, device=dev) for _ in range(L)]
+    lists = [(torch.empty((H, shard.n_pages), dtype=torch.int32, device=dev),
+              torch.empty((H,), dtype=torch.int32, device=dev)) for _ in range(L)]
     o_loc = torch.empty((L, 1, H * G, D), dtype=torch.float32, device=dev)
     lse_loc = torch.empty((L, 1, H * G), dtype=torch.float32, device=dev)
     o_out = torch.empty((L, H * G, D), dtype=torch.float32, device=dev)
@@ -242,7 +244,7 @@ def make_step(W, world, group, timing=None):
             if timing is not None:
                 timing["ev"][li][0].record()
             sel = fused.quest_select(pool, li, q_all[li], bt, sl, top_k=W["k"], sink_pages=shard.sink_pages,
-                                     scores=scores[li], thresh=thresh[li])
+                                     scores=scores[li], thresh=thresh[li], list_out=lists[li])
             if timing is not None:
                 timing["ev"][li][1].record()
             fused.decode(pool, li, q_all[li], bt, sl, sel, page_begin=shard.page_begin, n_splits=W["ns"],

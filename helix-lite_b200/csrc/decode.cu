@@ -24,7 +24,7 @@ constexpr int DS = 16;           // page size (tokens)
 constexpr int NW = 12;           // warps per CTA (one CTA per SM)
 constexpr int NT = NW * 32;
 constexpr int NSTAGE = 3;        // pages in smem per warp (two in flight while one is used)
-constexpr int LISTCAP = 256;     // pages gathered per round
+constexpr int LISTCAP = 512;     // pages gathered per round
 constexpr int ENTCAP = 128;      // outlier entries staged per page per K|V
 constexpr int SEGMAX = DS * DD;  // codes bytes per page segment at 4+4 bits
 constexpr int PSZ = 8 * DD + 16; // floats per split partial: O[8][128], m[8], l[8]
@@ -55,18 +55,19 @@ struct DecodeParams {
   uint32_t* err;
 };
 
-struct __align__(128) WarpSmem {
+struct __align__(256) WarpSmem {
   uint8_t raw[NSTAGE][SEGMAX];          // code segments
   uint32_t ent[NSTAGE][2][ENTCAP];      // [stage][K|V] outlier entries
   uint16_t tile[DS * DD];               // dequantised K, then V (swizzled rows)
-  uint16_t vlut[DS * 16];               // per-token V levels of the current page
+  alignas(256) uint16_t vlut[DS * 16];  // per-token V levels of the current page (256-aligned)
+  alignas(256) uint16_t vp[NSTAGE][DS * 16];  // per-token V levels copied with each page's codes
   uint64_t bar[NSTAGE];
 };
 
-struct __align__(128) CtaSmem {
+struct __align__(256) CtaSmem {
   WarpSmem w[NW];
-  uint16_t klut[16 * DD + 64];          // per-channel K levels (bank-spread)
-  uint16_t vtail[16];                   // V levels at positions >= t_cal
+  alignas(256) uint16_t klut[16 * DD + 64];  // per-channel K levels (bank-spread, 256-aligned)
+  alignas(256) uint16_t vtail[16];           // V levels at positions >= t_cal (256-aligned)
   int32_t pages[LISTCAP];
   int32_t phys[LISTCAP];
   uint4 dir[LISTCAP][2];                // K and V directory records of each page
@@ -76,15 +77,72 @@ struct __align__(128) CtaSmem {
   int32_t last;
 };
 
+// LUT dequant helpers. A table of 2-byte levels sits 256-aligned in smem; the
+// element's byte (2 * code, with the lane's table-offset low bits OR-ed in)
+// replaces the low byte of the table's base address in one prmt, and the
+// load carries the per-channel offset as its immediate.
+HX_DEVINL uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+HX_DEVINL uint16_t lds16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+
+// 8 levels for 8 consecutive 4-bit codes of word w (channels c0 .. c0+7):
+// tab(c) = base + off + TSTRIDE * (c - c0). Only base's low byte is replaced,
+// so off (a multiple of the table span, folded into the load's immediate once
+// unrolled) must be added after the prmt.
+template <int TSTRIDE>
+HX_DEVINL uint4 lut8_nib(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t off) {
+  const uint32_t lo = ((w << 1) & 0x1E1E1E1Eu) | lowbits;  // 2 * code of nibbles 0, 2, 4, 6
+  const uint32_t hi = ((w >> 3) & 0x1E1E1E1Eu) | lowbits;  // nibbles 1, 3, 5, 7
+  uint16_t v[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[2 * k] = lds16(prmt(lo, base, 0x7650u | k) + off + TSTRIDE * (2 * k));
+    v[2 * k + 1] = lds16(prmt(hi, base, 0x7650u | k) + off + TSTRIDE * (2 * k + 1));
+  }
+  return make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
+                    pack_u16x2(v[6], v[7]));
+}
+
+// 16 levels for 16 consecutive 2-bit codes of word w, as two 8-wide chunks.
+template <int TSTRIDE>
+HX_DEVINL void lut16_crumb(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t off, uint4& o0,
+                           uint4& o1) {
+  uint32_t g[4];
+  g[0] = ((w << 1) & 0x06060606u) | lowbits;  // crumbs 0, 4, 8, 12
+  g[1] = ((w >> 1) & 0x06060606u) | lowbits;  // crumbs 1, 5, 9, 13
+  g[2] = ((w >> 3) & 0x06060606u) | lowbits;  // crumbs 2, 6, 10, 14
+  g[3] = ((w >> 5) & 0x06060606u) | lowbits;  // crumbs 3, 7, 11, 15
+  uint16_t v[16];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int sft = 0; sft < 4; ++sft)
+      v[4 * k + sft] = lds16(prmt(g[sft], base, 0x7650u | k) + off + TSTRIDE * (4 * k + sft));
+  o0 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]), pack_u16x2(v[6], v[7]));
+  o1 = make_uint4(pack_u16x2(v[8], v[9]), pack_u16x2(v[10], v[11]), pack_u16x2(v[12], v[13]),
+                  pack_u16x2(v[14], v[15]));
+}
+
 // element offset of (token t, channel d) in a swizzled tile: 16-byte chunks
 // of a row are XOR-permuted by t & 7 so ldmatrix rows hit distinct banks
 HX_DEVINL int tile_off(int t, int d) { return t * DD + ((((d >> 3) ^ (t & 7))) << 3) + (d & 7); }
 
 template <int BK, int BV>
 __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   CtaSmem& sm = *reinterpret_cast<CtaSmem*>(smem_raw);
   constexpr int NLK = 1 << BK, NLV = 1 << BV;
+  if ((smem_u32(smem_raw) & 255u) != 0u) {  // the LUT address trick needs 256-aligned tables
+    if (threadIdx.x == 0) set_err(p.err, HX_DEV_ERR_BOUNDS);
+    return;
+  }
   constexpr int RBK = DD * BK / 8, RBV = DD * BV / 8;
   constexpr int SEG = DS * (RBK + RBV);
 
@@ -146,6 +204,14 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   const int sinks = min(max(p.sinks_req, 0), n);
   const uint64_t T = p.sel_mode == HX_SEL_THRESHOLD ? p.thresh[bh] : 0ull;
   const float* sc_bh = p.scores ? p.scores + (int64_t)bh * p.max_pages : nullptr;
+  // a page whose 16 tokens all lie before t_cal gets its per-token V levels by
+  // bulk copy with its codes when the rows are contiguous and 16-byte aligned
+  auto v_rows = [&](int pos0) -> const uint16_t* {
+    return p.sc.v_poles + ((int64_t)h * Tc + pos0) * NLV;
+  };
+  auto v_bulk = [&](int pos0) -> bool {
+    return pos0 + DS <= Tc && p.sc.levels_v == NLV && (reinterpret_cast<uintptr_t>(v_rows(pos0)) & 15u) == 0;
+  };
   __syncthreads();
 
   for (int rb = ra; rb < re; rb += LISTCAP) {
@@ -215,11 +281,15 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
         const uint4 dk = sm.dir[li][0], dv = sm.dir[li][1];
         const uint32_t ek = min((dk.z + 3u) & ~3u, (uint32_t)ENTCAP);
         const uint32_t ev = min((dv.z + 3u) & ~3u, (uint32_t)ENTCAP);
+        const int pos0 = (p.page_begin + sm.pages[li]) * DS;
+        const bool vb = v_bulk(pos0);
+        constexpr uint32_t VPB = 2u * DS * NLV;
         fence_proxy_async();
-        mbar_arrive_expect_tx(&ws.bar[st], SEG + 4u * (ek + ev));
+        mbar_arrive_expect_tx(&ws.bar[st], SEG + 4u * (ek + ev) + (vb ? VPB : 0u));
         bulk_g2s(ws.raw[st], p.pool.codes + ((int64_t)h * NB + pp) * SEG, SEG, &ws.bar[st]);
         if (ek) bulk_g2s(ws.ent[st][0], p.pool.arena + dk.x, 4u * ek, &ws.bar[st]);
         if (ev) bulk_g2s(ws.ent[st][1], p.pool.arena + dv.x, 4u * ev, &ws.bar[st]);
+        if (vb) bulk_g2s(ws.vp[st], v_rows(pos0), VPB, &ws.bar[st]);
       }
     };
 
@@ -245,40 +315,31 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       const int valid = seq_len - j * DS;  // tokens of this page inside the sequence
 
       const int t = lane & 15, half = lane >> 4;
-      // ---- K tile: per-channel LUT
+      // ---- K tile: per-channel LUT (lane = token t, half of the channels)
       {
         const uint8_t* rowp = ws.raw[st] + t * RBK + half * (RBK / 2);
-        const uint16_t* kl = sm.klut + half * (64 * NLK + 32);
+        // half 1's tables start 64 tables + 64 bytes later: its low address byte is 0x40
+        const uint32_t kbase = smem_u32(sm.klut) + (half ? (uint32_t)(64 * 2 * NLK + 64) : 0u);
+        const uint32_t low = half ? 0x40404040u : 0u;
         if (BK == 4) {
-          uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
-          uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
-          uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
+          const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
           for (int w8 = 0; w8 < 8; ++w8) {
-            uint16_t v[8];
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) v[jj] = kl[16 * (8 * w8 + jj) + ((wv[w8] >> (4 * jj)) & 15u)];
-            uint4 o4 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
-                                  pack_u16x2(v[6], v[7]));
+            const uint4 o4 = lut8_nib<32>(wv[w8], low, kbase, 32u * 8u * (uint32_t)w8);
             const int chunk = (8 * half + w8) ^ (t & 7);
             *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
           }
         } else {
-          uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
-          uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
 #pragma unroll
           for (int w4 = 0; w4 < 4; ++w4) {
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              uint16_t v[8];
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj)
-                v[jj] = kl[4 * (16 * w4 + 8 * hh + jj) + ((wv[w4] >> (2 * (8 * hh + jj))) & 3u)];
-              uint4 o4 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
-                                    pack_u16x2(v[6], v[7]));
-              const int chunk = (8 * half + 2 * w4 + hh) ^ (t & 7);
-              *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
-            }
+            uint4 o0, o1;
+            lut16_crumb<8>(wv[w4], low, kbase, 8u * 16u * (uint32_t)w4, o0, o1);
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4) ^ (t & 7)) * 8)) = o0;
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4 + 1) ^ (t & 7)) * 8)) = o1;
           }
         }
       }
@@ -339,50 +400,51 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       const uint32_t bl0 = movmatrix_trans(plo_top), bl1 = movmatrix_trans(plo_bot);
 
       // ---- V tile: per-token LUT (row min(pos, t_cal - 1))
-      const uint16_t* vl;
+      uint32_t vbase, vlow;
       if (pos0 >= Tc) {
-        vl = sm.vtail;
+        vbase = smem_u32(sm.vtail);  // one table for every token
+        vlow = 0u;
       } else {
-        for (int i = lane; i < DS * NLV; i += 32) {
-          int r = i / NLV, c = i % NLV;
-          int pr = min(pos0 + r, Tc - 1);
-          ws.vlut[r * NLV + c] =
-              c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + pr) * p.sc.levels_v + c] : (uint16_t)0;
+        if (v_bulk(pos0)) {
+          vbase = smem_u32(ws.vp[st]);
+        } else {
+          uint16_t lv[DS * NLV / 32];
+#pragma unroll
+          for (int u = 0; u < DS * NLV / 32; ++u) {
+            const int i = lane + 32 * u;
+            const int r = i / NLV, c = i % NLV;
+            const int pr = min(pos0 + r, Tc - 1);
+            lv[u] = c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + pr) * p.sc.levels_v + c] : (uint16_t)0;
+          }
+#pragma unroll
+          for (int u = 0; u < DS * NLV / 32; ++u) ws.vlut[lane + 32 * u] = lv[u];
+          __syncwarp();
+          vbase = smem_u32(ws.vlut);
         }
-        __syncwarp();
-        vl = ws.vlut + t * NLV;
+        vbase += 2u * NLV * (uint32_t)t;  // token t's table
+        vlow = ((2u * NLV * (uint32_t)t) & 0xFFu) * 0x01010101u;
       }
       {
         const uint8_t* rowp = ws.raw[st] + DS * RBK + t * RBV + half * (RBV / 2);
         if (BV == 4) {
-          uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
-          uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
-          uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
+          const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
           for (int w8 = 0; w8 < 8; ++w8) {
-            uint16_t v[8];
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) v[jj] = vl[(wv[w8] >> (4 * jj)) & 15u];
-            uint4 o4 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
-                                  pack_u16x2(v[6], v[7]));
+            const uint4 o4 = lut8_nib<0>(wv[w8], vlow, vbase, 0u);
             const int chunk = (8 * half + w8) ^ (t & 7);
             *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
           }
         } else {
-          uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
-          uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
 #pragma unroll
           for (int w4 = 0; w4 < 4; ++w4) {
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              uint16_t v[8];
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj) v[jj] = vl[(wv[w4] >> (2 * (8 * hh + jj))) & 3u];
-              uint4 o4 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
-                                    pack_u16x2(v[6], v[7]));
-              const int chunk = (8 * half + 2 * w4 + hh) ^ (t & 7);
-              *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
-            }
+            uint4 o0, o1;
+            lut16_crumb<0>(wv[w4], vlow, vbase, 0u, o0, o1);
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4) ^ (t & 7)) * 8)) = o0;
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4 + 1) ^ (t & 7)) * 8)) = o1;
           }
         }
       }

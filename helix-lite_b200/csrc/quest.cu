@@ -667,6 +667,101 @@ __global__ void __launch_bounds__(1024) quest_compact_kernel(const float* scores
   if (threadIdx.x == 0) counts[row] = min(s_base, max_out);
 }
 
+// Chunked list compaction for the decode: many CTAs per (b, h). Pass 1 counts
+// the selected pages of each chunk of kListChunk pages; pass 2 sums the counts
+// of the chunks before its own and writes its pages at that offset, so the
+// list comes out ascending and identical run to run.
+constexpr int kListChunk = 2048;
+constexpr int kListThreads = 256;
+constexpr int kListPer = kListChunk / kListThreads;  // consecutive pages per thread
+
+HX_DEVINL int chunk_pages_n(const int32_t* seq_lens, int b, int S, int max_pages) {
+  return min((seq_lens[b] + S - 1) / S, max_pages);
+}
+
+// selected-page bitmask of this thread's kListPer consecutive pages
+HX_DEVINL uint32_t chunk_thread_mask(const float* sc, uint64_t T, int j0, int n, int sinks) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < kListPer; ++i) {
+    const int j = j0 + i;
+    if (j < n && (j < sinks || order_key64(__ldg(sc + j), (uint32_t)j) >= T)) m |= 1u << i;
+  }
+  return m;
+}
+
+__global__ void __launch_bounds__(kListThreads) quest_list_count_kernel(const float* scores, const uint64_t* thresh,
+                                                                       int H, const int32_t* seq_lens, int S,
+                                                                       int max_pages, int sinks_req, int nch,
+                                                                       int32_t* chunk_counts) {
+  __shared__ int s_w[kListThreads / 32];
+  const int row = blockIdx.y, c = blockIdx.x;
+  const int n = chunk_pages_n(seq_lens, row / H, S, max_pages);
+  const int sinks = min(max(sinks_req, 0), n);
+  const int j0 = c * kListChunk + threadIdx.x * kListPer;
+  const uint32_t m = chunk_thread_mask(scores + (int64_t)row * max_pages, thresh[row], j0, n, sinks);
+  int cnt = __popc(m);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if ((threadIdx.x & 31) == 0) s_w[threadIdx.x >> 5] = cnt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < kListThreads / 32; ++w) t += s_w[w];
+    chunk_counts[(int64_t)row * nch + c] = t;
+  }
+}
+
+__global__ void __launch_bounds__(kListThreads) quest_list_scatter_kernel(
+    const float* scores, const uint64_t* thresh, int H, const int32_t* seq_lens, int S, int max_pages,
+    int sinks_req, int nch, const int32_t* chunk_counts, int max_out, int32_t* out, int32_t* counts) {
+  __shared__ int s_w[kListThreads / 32];
+  __shared__ int s_base;
+  const int row = blockIdx.y, c = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = chunk_pages_n(seq_lens, row / H, S, max_pages);
+  const int sinks = min(max(sinks_req, 0), n);
+  // offset of this chunk: the counts of the chunks before it
+  int pre = 0;
+  for (int i = threadIdx.x; i < c; i += kListThreads) pre += chunk_counts[(int64_t)row * nch + i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) pre += __shfl_xor_sync(0xffffffffu, pre, o);
+  if (lane == 0) s_w[warp] = pre;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < kListThreads / 32; ++w) t += s_w[w];
+    s_base = t;
+  }
+  __syncthreads();
+  const int base = s_base;
+  const int j0 = c * kListChunk + threadIdx.x * kListPer;
+  const uint32_t m = chunk_thread_mask(scores + (int64_t)row * max_pages, thresh[row], j0, n, sinks);
+  const int cnt = __popc(m);
+  // exclusive scan of the per-thread counts (threads hold consecutive pages)
+  int inc = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  __syncthreads();
+  if (lane == 31) s_w[warp] = inc;
+  __syncthreads();
+  int woff = 0;
+  for (int w = 0; w < warp; ++w) woff += s_w[w];
+  int pos = base + woff + inc - cnt;
+  int32_t* orow = out + (int64_t)row * max_out;
+#pragma unroll
+  for (int i = 0; i < kListPer; ++i) {
+    if ((m >> i) & 1u) {
+      if (pos < max_out) orow[pos] = j0 + i;
+      ++pos;
+    }
+  }
+  if (c == nch - 1 && threadIdx.x == kListThreads - 1) counts[row] = min(pos, max_out);
+}
+
 }  // namespace hx
 
 // ===========================================================================
@@ -790,6 +885,28 @@ HX_API int hx_quest_compact(void* stream, const float* scores, const uint64_t* t
   int rows = union_heads ? B : B * H;
   quest_compact_kernel<<<rows, 1024, 0, S_(stream)>>>(scores, thresh, H, seq_lens, page_size, max_pages, sink_pages,
                                                       union_heads, max_out, out, counts);
+  HX_LAUNCH_CHECK();
+  return HX_OK;
+}
+
+HX_API int hx_quest_lists(void* stream, const float* scores, const uint64_t* thresh, int32_t B, int32_t H,
+                          const int32_t* seq_lens, int32_t page_size, int32_t max_pages, int32_t sink_pages,
+                          int32_t max_out, int32_t* out, int32_t* counts, int32_t* chunk_counts) {
+  if (B < 0 || H <= 0 || page_size <= 0 || max_pages < 0 || max_out < 0) return HX_ERR_ARG;
+  if (B == 0) return HX_OK;
+  if (!scores || !thresh || !seq_lens || !counts || (max_out > 0 && !out)) return HX_ERR_ARG;
+  const int nch = max(1, (max_pages + kListChunk - 1) / kListChunk);
+  if (nch > 1 && !chunk_counts) return HX_ERR_ARG;
+  if ((int64_t)B * H > 65535) return HX_ERR_UNSUPPORTED;
+  dim3 grid(nch, B * H);
+  if (nch > 1) {
+    quest_list_count_kernel<<<grid, kListThreads, 0, S_(stream)>>>(scores, thresh, H, seq_lens, page_size,
+                                                                   max_pages, sink_pages, nch, chunk_counts);
+    HX_LAUNCH_CHECK();
+  }
+  quest_list_scatter_kernel<<<grid, kListThreads, 0, S_(stream)>>>(scores, thresh, H, seq_lens, page_size,
+                                                                   max_pages, sink_pages, nch, chunk_counts,
+                                                                   max_out, out, counts);
   HX_LAUNCH_CHECK();
   return HX_OK;
 }

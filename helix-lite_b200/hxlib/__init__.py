@@ -57,6 +57,7 @@ _SIGS = {
                                    c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "hx_quest_compact": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32,
                                  c_vp, c_vp]),
+    "hx_quest_lists": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]),
     "hx_decode_scratch_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "hx_decode_attn": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_i32, c_i32, c_f32, c_vp, c_i32,
                                c_vp, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_vp, c_i32, c_vp, c_i32,
@@ -101,7 +102,7 @@ def lib():
 LAUNCHES = {"hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 1, "hx_unpack_pages": 1,
             "hx_nuq_pack_dense": 1, "hx_nuq_unpack_dense": 1, "hx_nuq_quantize_flat": 2,
             "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": 1,
-            "hx_quest_compact": 1, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_merge_partials": 1,
+            "hx_quest_compact": 1, "hx_quest_lists": 2, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_merge_partials": 1,
             "hx_selected_attention": 1}
 launch_count = [0]
 

@@ -12,6 +12,11 @@ fp16 staging buffer (src/kvquant/compact_backend.py:225-299):
                  normalised o (fp32) and lse (natural log)
   selected_lists the selection as ascending page lists (API / tests)
 
+quest_select also writes the selection as ascending per-(b, h) page lists
+(two bandwidth-bound passes over the scores), and decode balances its splits
+over those lists, so every CTA gets the same number of selected pages however
+the selection clusters along the sequence.
+
 Everything is asynchronous on the current stream; scratch is cached per
 device and left zeroed by the kernels.
 """
@@ -38,6 +43,8 @@ class Selection:
     page_size: int
     max_pages: int
     sink_pages: int
+    lists: torch.Tensor | None = None   # (B * H, max_pages) int32 ascending selected pages
+    counts: torch.Tensor | None = None  # (B * H,) int32
 
 
 def _i32(t, device):
@@ -47,7 +54,8 @@ def _i32(t, device):
 def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
                  seq_lens: torch.Tensor, *, top_k: int | None = None, top_frac=(1, 4), sink_pages: int = 4,
                  gqa: str = "sum", max_pages: int | None = None, scores: torch.Tensor | None = None,
-                 thresh: torch.Tensor | None = None) -> Selection:
+                 thresh: torch.Tensor | None = None, lists: bool = True,
+                 list_out: tuple[torch.Tensor, torch.Tensor] | None = None) -> Selection:
     """Score every page of each sequence and fix the exact top-K thresholds.
 
     query (B, Hq, D) fp16 with Hq = group * H; block_table (B, >= max_pages)
@@ -56,7 +64,9 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
     k = top_k pages if given,
     else floor(n_pages * top_frac[0] / top_frac[1]); gqa "sum" adds the
     per-query-head bounds of a group, "mean" bounds the group's mean query
-    (the reference hook, compact_backend.py:231).
+    (the reference hook, compact_backend.py:231). ``lists`` also writes the
+    ascending page lists the decode balances over, into ``list_out`` =
+    ((B*H, max_pages) int32, (B*H,) int32) when given.
     """
     dev = pool.device
     q = query.to(device=dev, dtype=torch.float16).contiguous()
@@ -85,7 +95,21 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
         kf, fn, fd = (int(top_k), 0, 0) if top_k is not None else (0, int(top_frac[0]), int(top_frac[1]))
         call("hx_quest_threshold", st, ptr(scores), B, H, ptr(sl), S, mp, sink_pages, kf, fn, fd, 1, ptr(hist),
              ptr(cand), ptr(ctr), ptr(thresh), ptr(hxlib.err_word(dev)))
-    return Selection(scores, thresh, sl, S, mp, sink_pages)
+        lst = cnt = None
+        if lists:
+            mpl = max(mp, 1)
+            if list_out is not None:
+                lst, cnt = list_out
+            else:
+                lst = torch.empty((B * H, mpl), dtype=torch.int32, device=dev)
+                cnt = torch.empty((B * H,), dtype=torch.int32, device=dev)
+            if lst.shape != (B * H, mpl) or cnt.shape != (B * H,) or lst.dtype != torch.int32:
+                raise ValueError("list_out must be ((B*H, max_pages) int32, (B*H,) int32)")
+            nch = -(-mpl // 2048)
+            chunks = hxlib.scratch(dev, "quest_chunks", B * H * nch * 4)
+            call("hx_quest_lists", st, ptr(scores), ptr(thresh), B, H, ptr(sl), S, mp, sink_pages, mpl, ptr(lst),
+                 ptr(cnt), ptr(chunks))
+    return Selection(scores, thresh, sl, S, mp, sink_pages, lst, cnt)
 
 
 def selected_lists(sel: Selection, union: bool = False, max_out: int | None = None):
@@ -130,7 +154,11 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
     bt = _i32(block_table, dev)
     sl = _i32(seq_lens, dev)
     mp = int(max_pages if max_pages is not None else bt.shape[1])
-    if selection is not None:
+    if selection is not None and selection.lists is not None and lists is None:
+        lists, list_counts = selection.lists, selection.counts
+        mode = SEL_LIST
+        selection = None
+    elif selection is not None:
         mp = selection.max_pages  # the scores' row stride
         mode = SEL_THRESHOLD
     elif lists is not None:

@@ -207,6 +207,20 @@ HX_API int hx_quest_compact(void* stream, const float* scores, const uint64_t* t
                             int32_t max_pages, int32_t sink_pages, int32_t union_heads,
                             int32_t max_out, int32_t* out, int32_t* counts);
 
+/* The same per-(b, h) ascending lists as hx_quest_compact without the union,
+ * written by ceil(max_pages / HX_LIST_CHUNK) CTAs per (b, h) in two passes so
+ * that long sequences are compacted at full bandwidth; this is the list the
+ * decode balances its splits over (HX_SEL_LIST). chunk_counts: scratch of
+ * B*H*ceil(max_pages / HX_LIST_CHUNK) int32 (no initial value; may be NULL
+ * when max_pages <= HX_LIST_CHUNK). No reference counterpart: the reference
+ * selects with torch.topk and hands FlashAttention a page list
+ * (src/kvquant/quest_selector.py:38-97). */
+#define HX_LIST_CHUNK 2048
+HX_API int hx_quest_lists(void* stream, const float* scores, const uint64_t* thresh,
+                          int32_t B, int32_t H, const int32_t* seq_lens, int32_t page_size,
+                          int32_t max_pages, int32_t sink_pages, int32_t max_out,
+                          int32_t* out, int32_t* counts, int32_t* chunk_counts);
+
 /* ---- fused-dequant decode attention (Kernel C) ------------------------ */
 
 #define HX_SEL_DENSE     0   /* every page of the sequence                  */

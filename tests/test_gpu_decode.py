@@ -100,6 +100,12 @@ def test_quest_decode_matches_oracle_config3_shape():
     ro, rl = _oracle_out(orc, 0, q, bt, sl, [pages])
     assert np.abs(np16(o) - ro).max() < TOL
     np.testing.assert_allclose(np16(lse), rl, atol=1e-3)
+    # the same selection read from the thresholds instead of the lists
+    sel_t = fused.quest_select(gpu, 0, q, bt, sl, top_frac=(1, 4), sink_pages=4, lists=False)
+    o_t, lse_t = fused.decode(gpu, 0, q, bt, sl, sel_t)
+    gpu.check()
+    assert np.abs(np16(o_t) - ro).max() < TOL
+    np.testing.assert_allclose(np16(lse_t), rl, atol=1e-3)
 
 
 def test_batched_decode_block_tables_partial_pages():

@@ -71,6 +71,9 @@ def test_selection_edge_sizes(P, k, sinks):
         want = oq.select_pages(ref[:, h], k, sinks)
         assert int(counts[0, h]) == len(want)
         np.testing.assert_array_equal(np16(lists[0, h, :len(want)]), want)
+        # the chunked lists the decode balances over (hx_quest_lists)
+        assert int(sel.counts[h]) == len(want)
+        np.testing.assert_array_equal(np16(sel.lists[h, :len(want)]), want)
 
 
 def test_selection_ties_go_to_lower_page():
@@ -113,6 +116,8 @@ def test_batched_selection_with_block_tables_and_union():
             want = oq.select_pages(ref[:, h], n // 4, 4)
             union |= set(want.tolist())
             np.testing.assert_array_equal(np16(lists[b, h, :int(counts[b, h])]), want)
+            assert int(sel.counts[b * H + h]) == len(want)
+            np.testing.assert_array_equal(np16(sel.lists[b * H + h, :len(want)]), want)
         np.testing.assert_array_equal(np16(ulists[b, :int(ucounts[b])]), sorted(union))
 
 
