@@ -8,41 +8,31 @@
 // src/quest/reference.py:136-168 (softmax(q.K^T * scale) V, fp32 softmax),
 // generalised to grouped-query heads (query head h*G+g reads KV head h).
 //
-// One CTA = (split, KV head, sequence) on one SM, warp-specialised:
-//   producer warp   walks the CTA's page list: one bulk copy (cp.async.bulk,
-//                   no multicast) per page for its code segment (and, before
-//                   t_cal, its per-token V level rows), cp.async for its
-//                   outlier entries, into a ring of NRAW page slots;
-//   dequant warps   NDQ warps take every NDQ-th page: LUT dequant of K and V
-//                   into swizzled fp16 tiles, outlier patch, release the page
-//                   slot, publish the tiles (ring of NTILE tile pairs);
-//   MMA warps       NMM warps each own every NMM-th page: ldmatrix + mma.sync
-//                   S = K.Q^T (tokens x GQA heads), online softmax in fp32
-//                   (exp2 domain, the running max raised only when a score
-//                   passes it by 2^8), P split into fp16 hi + lo so P.V keeps
-//                   ~22 bits, O^T += V^T.P^T.
-// The MMA warps merge in smem; the last CTA of each (b, h) merges the splits.
-// Every wait is bounded: a wait that runs out sets HX_DEV_ERR_TIMEOUT and an
-// abort flag that ends the other roles' loops.
+// One CTA = (split, KV head, sequence), 12 warps, one CTA per SM; the CTA's
+// pages (a balanced share of the selected list) are dealt to the warps. Each
+// warp streams its pages: bulk copies (cp.async.bulk, no multicast) of the
+// page's code segment, its outlier entries and, before t_cal, its per-token V
+// level rows into a 3-stage buffer; LUT dequant of the 16 x 128 K tile into
+// swizzled smem (one prmt-built table address per code), outlier patch,
+// ldmatrix + mma.sync (tokens x heads), online softmax in fp32 (exp2 domain;
+// the running max moves only when a score passes it by 2^8), P split into
+// fp16 hi + lo parts so P.V keeps ~22 bits, V tile the same way, PV with two
+// MMAs per m-tile. Warps merge in smem; the last CTA of each (b, h) merges
+// the splits.
 #include "common.cuh"
 
 namespace hx {
 
 constexpr int DD = 128;          // head_size
 constexpr int DS = 16;           // page size (tokens)
-constexpr int NDQ = 15;          // dequant warps
-constexpr int NMM = 7;           // MMA / softmax warps
-constexpr int NWARP = 1 + NDQ + NMM;
-constexpr int NT = NWARP * 32;
-constexpr int NRAW = 16;         // page slots: codes + outlier entries + V level rows
-constexpr int NTILE = 14;        // dequantised K|V tile slots (two per MMA warp)
-constexpr int PB = 8;            // pages the producer starts per batch (4 lanes each)
+constexpr int NW = 12;           // warps per CTA (one CTA per SM)
+constexpr int NT = NW * 32;
+constexpr int NSTAGE = 3;        // pages in smem per warp (two in flight while one is used)
 constexpr int LISTCAP = 512;     // pages gathered per round
 constexpr int ENTCAP = 128;      // outlier entries staged per page per K|V
 constexpr int SEGMAX = DS * DD;  // codes bytes per page segment at 4+4 bits
 constexpr int PSZ = 8 * DD + 16; // floats per split partial: O[8][128], m[8], l[8]
 constexpr int MAXSPLIT = 1024;   // splits the final merge stages weights for
-static_assert(PB == 8 && PB <= NRAW, "a producer batch: 8 distinct page slots, 4 lanes a page");
 
 struct DecodeParams {
   hx_pool_layer pool;
@@ -69,41 +59,31 @@ struct DecodeParams {
   uint32_t* err;
 };
 
-
-struct __align__(256) RawSlot {
-  uint8_t codes[SEGMAX];              // K rows then V rows of one (head, page) segment
-  uint32_t ent[2][ENTCAP];            // K | V outlier entries
-  alignas(256) uint16_t vp[DS * 16];  // per-token V levels (pages before t_cal)
-};
-
-struct __align__(256) TileSlot {
-  uint16_t k[DS * DD];  // dequantised K, swizzled rows
-  uint16_t v[DS * DD];  // dequantised V, swizzled rows
-};
-
-struct __align__(256) DqSmem {
-  uint32_t ent[2][ENTCAP];            // the page's K | V outlier entries
-  alignas(256) uint16_t vlut[DS * 16];  // the page's per-token V levels (before t_cal)
+struct __align__(256) WarpSmem {
+  uint8_t raw[NSTAGE][SEGMAX];          // code segments
+  uint32_t ent[NSTAGE][2][ENTCAP];      // [stage][K|V] outlier entries
+  uint16_t tile[DS * DD];               // dequantised K, then V (swizzled rows)
+  alignas(256) uint16_t vlut[DS * 16];  // per-token V levels of the current page (256-aligned)
+  alignas(256) uint16_t vp[NSTAGE][DS * 16];  // per-token V levels copied with each page's codes
+  uint64_t bar[NSTAGE];
 };
 
 struct __align__(256) CtaSmem {
-  RawSlot raw[NRAW];
-  TileSlot tile[NTILE];                      // raw + tile also hold the merges' buffers
+  WarpSmem w[NW];
   alignas(256) uint16_t klut[16 * DD + 64];  // per-channel K levels (bank-spread, 256-aligned)
   alignas(256) uint16_t vtail[16];           // V levels at positions >= t_cal (256-aligned)
-  DqSmem dq[NDQ];                            // per dequant warp
   int32_t pages[LISTCAP];
   int32_t phys[LISTCAP];
-  uint4 dir[LISTCAP][2];                     // K and V directory records of each page
-  uint64_t raw_full[NRAW], raw_empty[NRAW], tile_full[NTILE], tile_empty[NTILE];
-  float wml[NMM][16];                        // per MMA warp: m[8], l[8]
-  float colM[8], colL[8];
+  uint4 dir[LISTCAP][2];                // K and V directory records of each page
+  float colM[8], colL[8];               // per-column max / sum for the merges
   int32_t count;
-  int32_t wcount[NWARP];
+  int32_t wcount[NW];
   int32_t last;
-  int32_t abort_flag;
 };
 
+// LUT dequant helpers. A table of 2-byte levels sits 256-aligned in smem; the
+// element's byte (2 * code, with the lane's table-offset low bits OR-ed in)
+// replaces the low byte of the table's base address in one prmt, and the
 // load carries the per-channel offset as its immediate.
 HX_DEVINL uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
@@ -158,77 +138,29 @@ HX_DEVINL void lut16_crumb(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t
 // of a row are XOR-permuted by t & 7 so ldmatrix rows hit distinct banks
 HX_DEVINL int tile_off(int t, int d) { return t * DD + ((((d >> 3) ^ (t & 7))) << 3) + (d & 7); }
 
-
-// 16-byte global -> shared copy through the load path (L2 only)
-HX_DEVINL void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-
-// arrive on an mbarrier once all of this thread's earlier cp.async have landed
-HX_DEVINL void cp_async_arrive(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-HX_DEVINL void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-HX_DEVINL void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Bounded wait of one thread; gives up early once another role has aborted.
-// Each poll suspends the thread until the phase completes or kSuspendNs pass,
-// then backs off briefly, so an idle role costs few issue slots; kRolePolls
-// polls bound the wait to about two seconds.
-constexpr uint32_t kSuspendNs = 1u << 19;
-constexpr uint32_t kRolePolls = 1u << 12;
-HX_DEVINL bool role_wait(uint64_t* bar, uint32_t parity, volatile int32_t* abort_flag, uint32_t* err) {
-  const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < kRolePolls; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n"
-        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-        " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(addr), "r"(parity), "r"(kSuspendNs)
-        : "memory");
-    if (done) return true;
-    if (*abort_flag) return false;
-    __nanosleep(20u << min(i, 4u));  // back off: waiting warps leave issue slots to working ones
-  }
-  set_err(err, HX_DEV_ERR_TIMEOUT);
-  *abort_flag = 1;
-  return false;
-}
-
-// The same for a whole warp: every lane acquires; the answer is warp-uniform.
-HX_DEVINL bool warp_wait(uint64_t* bar, uint32_t parity, volatile int32_t* abort_flag, uint32_t* err) {
-  return __all_sync(0xffffffffu, role_wait(bar, parity, abort_flag, err));
-}
-
 template <int BK, int BV>
 __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   CtaSmem& sm = *reinterpret_cast<CtaSmem*>(smem_raw);
   constexpr int NLK = 1 << BK, NLV = 1 << BV;
-  constexpr int RBK = DD * BK / 8, RBV = DD * BV / 8;  // bytes per token row
-  constexpr uint32_t SEG = DS * (RBK + RBV);
-  constexpr uint32_t VPB = 2u * DS * NLV;              // V level rows of one page
   if ((smem_u32(smem_raw) & 255u) != 0u) {  // the LUT address trick needs 256-aligned tables
     if (threadIdx.x == 0) set_err(p.err, HX_DEV_ERR_BOUNDS);
     return;
   }
+  constexpr int RBK = DD * BK / 8, RBV = DD * BV / 8;
+  constexpr int SEG = DS * (RBK + RBV);
+
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int H = gridDim.y, G = p.G;
+  const int H = p.pool.num_kv_heads;
   const int bh = b * H + h;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.G;
   const int Tc = p.sc.t_cal;
   const int NB = p.pool.num_blocks;
   const int seq_len = p.seq_lens[b];
   const int n = min((seq_len + DS - 1) / DS, p.max_pages);
-  volatile int32_t* abort_flag = &sm.abort_flag;
 
-  // ---- per-CTA tables and barriers
+  // ---- per-CTA tables
   for (int i = tid; i < NLK * DD; i += NT) {
     int d = i / NLK, c = i % NLK;
     sm.klut[NLK * d + 32 * (d >> 6) + c] =
@@ -236,29 +168,20 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   }
   if (tid < NLV)
     sm.vtail[tid] = tid < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + (Tc - 1)) * p.sc.levels_v + tid] : (uint16_t)0;
-  if (tid == 0) {
-    for (int s = 0; s < NRAW; ++s) {
-      mbar_init(&sm.raw_full[s], 5);   // arrive.expect_tx + 4 lanes' cp.async arrivals
-      mbar_init(&sm.raw_empty[s], 1);  // the dequant warp
-    }
-    for (int s = 0; s < NTILE; ++s) {
-      mbar_init(&sm.tile_full[s], 1);  // the dequant warp
-      mbar_init(&sm.tile_empty[s], 1); // the MMA warp
-    }
-    sm.abort_flag = 0;
+  WarpSmem& ws = sm.w[warp];
+  if (lane == 0) {
+    for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
     fence_mbar_init();
   }
 
-  // ---- MMA warps: query fragments (B operand, k = channel, n = head column)
-  const bool is_mma = warp > NDQ;
-  const int mw = warp - 1 - NDQ;
+  // query fragments (B operand, k = channel, n = head column)
   const int g = lane >> 2, qd = lane & 3;
   uint32_t bq[8][2];
   {
     const int64_t qrow = ((int64_t)b * H * G + (int64_t)h * G + g) * DD;
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
-      if (is_mma && g < G) {
+      if (g < G) {
         bq[ks][0] = *reinterpret_cast<const uint32_t*>(p.q + qrow + 16 * ks + 2 * qd);
         bq[ks][1] = *reinterpret_cast<const uint32_t*>(p.q + qrow + 16 * ks + 2 * qd + 8);
       } else {
@@ -267,10 +190,14 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       }
     }
   }
+
   float oacc[8][4];
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.0f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  uint32_t phase = 0;     // bit s = parity to wait for on stage s
+  uint32_t inflight = 0;  // bit s = a bulk copy into stage s not yet waited for
+  bool timed_out = false;
 
   // ---- split range
   int total;
@@ -291,7 +218,6 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   };
   __syncthreads();
 
-  int done = 0;  // pages of earlier rounds: ring slot / phase of page k is (done + k)
   for (int rb = ra; rb < re; rb += LISTCAP) {
     const int rend = min(rb + LISTCAP, re);
     if (tid == 0) sm.count = 0;
@@ -340,296 +266,267 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       __syncthreads();
       if (tid == 0) {
         int c = sm.count;
-        for (int w = 0; w < NWARP; ++w) c += sm.wcount[w];
+        for (int w = 0; w < NW; ++w) c += sm.wcount[w];
         sm.count = c;
       }
       __syncthreads();
     }
     const int cnt = sm.count;
+    const int my_n = cnt > warp ? (cnt - warp + NW - 1) / NW : 0;
 
-    if (warp == 0) {
-      // ================= producer, PB = 8 pages a batch: lane i < 8 starts page
-      // k0 + i's code segment (and V level rows) as one bulk copy; lanes
-      // 4i .. 4i+3 copy its outlier entries with cp.async. A page's slot
-      // fills when the bulk bytes and those 4 lanes' cp.async have landed.
-      int issued = 0;
-      for (int k0 = 0; k0 < cnt; k0 += PB) {
-        if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-        const int k = k0 + lane;
-        const bool mine = lane < PB && k < cnt;
-        const int K = done + k, s = K % NRAW;
-        const uint32_t nr = (uint32_t)(K / NRAW);
-        const bool ok = !(mine && nr > 0) || role_wait(&sm.raw_empty[s], (nr - 1u) & 1u, abort_flag, p.err);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        if (mine) {
-          const int pp = sm.phys[k];
-          const int pos0 = (p.page_begin + sm.pages[k]) * DS;
-          const bool vb = v_bulk(pos0);
-          RawSlot& rs = sm.raw[s];
-          fence_proxy_async();
-          mbar_arrive_expect_tx(&sm.raw_full[s], SEG + (vb ? VPB : 0u));
-          bulk_g2s(rs.codes, p.pool.codes + ((int64_t)h * NB + pp) * SEG, SEG, &sm.raw_full[s]);
-          if (vb) bulk_g2s(rs.vp, v_rows(pos0), VPB, &sm.raw_full[s]);
-        }
-        // entries: lanes 4j .. 4j+3 copy page k0 + j's, 16 bytes at a time
-        const int nb = min(PB, cnt - k0);
-        const int j = lane >> 2, q = lane & 3;
-        if (j < nb) {
-          const int kj = k0 + j, sj = (done + kj) % NRAW;
-          const uint4 dk = sm.dir[kj][0], dv = sm.dir[kj][1];
-          const uint32_t ck = min((dk.z + 3u) >> 2, (uint32_t)ENTCAP / 4);
-          const uint32_t cv = min((dv.z + 3u) >> 2, (uint32_t)ENTCAP / 4);
-          RawSlot& rj = sm.raw[sj];
-          for (uint32_t c = q; c < ck; c += 4) cp_async16(&rj.ent[0][4 * c], p.pool.arena + dk.x + 4 * c);
-          for (uint32_t c = q; c < cv; c += 4) cp_async16(&rj.ent[1][4 * c], p.pool.arena + dv.x + 4 * c);
-          cp_async_arrive(&sm.raw_full[sj]);
-        }
-        issued = k0 + nb;
+    // ---- warp pipeline over pages warp, warp + NW, ...
+    auto issue = [&](int k) {
+      if (timed_out) return;
+      const int st = k % NSTAGE;
+      inflight |= 1u << st;
+      if (lane == 0) {
+        const int li = warp + NW * k;
+        const int pp = sm.phys[li];
+        const uint4 dk = sm.dir[li][0], dv = sm.dir[li][1];
+        const uint32_t ek = min((dk.z + 3u) & ~3u, (uint32_t)ENTCAP);
+        const uint32_t ev = min((dv.z + 3u) & ~3u, (uint32_t)ENTCAP);
+        const int pos0 = (p.page_begin + sm.pages[li]) * DS;
+        const bool vb = v_bulk(pos0);
+        constexpr uint32_t VPB = 2u * DS * NLV;
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&ws.bar[st], SEG + 4u * (ek + ev) + (vb ? VPB : 0u));
+        bulk_g2s(ws.raw[st], p.pool.codes + ((int64_t)h * NB + pp) * SEG, SEG, &ws.bar[st]);
+        if (ek) bulk_g2s(ws.ent[st][0], p.pool.arena + dk.x, 4u * ek, &ws.bar[st]);
+        if (ev) bulk_g2s(ws.ent[st][1], p.pool.arena + dv.x, 4u * ev, &ws.bar[st]);
+        if (vb) bulk_g2s(ws.vp[st], v_rows(pos0), VPB, &ws.bar[st]);
       }
-      cp_async_wait_all();
-      if (__any_sync(0xffffffffu, *abort_flag != 0) && lane == 0) {
-        // let the bulk copies still in flight land before the CTA moves on
-        for (int k = max(0, issued - NRAW); k < issued; ++k) {
-          const int K = done + k;
-          (void)mbar_wait(&sm.raw_full[K % NRAW], (uint32_t)(K / NRAW) & 1u);
+    };
+
+    for (int k = 0; k < NSTAGE - 1 && k < my_n; ++k) issue(k);
+    for (int k = 0; k < my_n; ++k) {
+      const int st = k % NSTAGE;
+      if (k + NSTAGE - 1 < my_n) issue(k + NSTAGE - 1);  // its stage held page k - 1, done
+      if (!timed_out) {
+        if (mbar_wait(&ws.bar[st], (phase >> st) & 1u)) {
+          phase ^= 1u << st;
+          inflight &= ~(1u << st);
+        } else {
+          timed_out = true;
+          if (lane == 0) set_err(p.err, HX_DEV_ERR_TIMEOUT);
         }
       }
-    } else if (!is_mma) {
-      // ================= dequant warps: pages dw, dw + NDQ, ... (K then V).
-      // The page's codes go to registers and its outlier entries (and V
-      // level rows) to the warp's own buffer first, so the page slot is
-      // released before the LUT work and the producer can refill it.
-      const int dw = warp - 1;
+      if (timed_out) continue;
+      const int li = warp + NW * k;
+      const uint4 dk = sm.dir[li][0], dv = sm.dir[li][1];
+      const uint32_t offk = dk.x, cntk = dk.z, offv = dv.x, cntv = dv.z;
+      const int j = sm.pages[li];
+      const int pos0 = (p.page_begin + j) * DS;
+      const int valid = seq_len - j * DS;  // tokens of this page inside the sequence
+
       const int t = lane & 15, half = lane >> 4;
-      DqSmem& dq = sm.dq[dw];
-      for (int k = dw; k < cnt; k += NDQ) {
-        if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-        const int K = done + k, s = K % NRAW, ts = K % NTILE;
-        const uint32_t nr = (uint32_t)(K / NRAW), nt = (uint32_t)(K / NTILE);
-        if (nt > 0 && !warp_wait(&sm.tile_empty[ts], (nt - 1u) & 1u, abort_flag, p.err)) break;
-        if (!warp_wait(&sm.raw_full[s], nr & 1u, abort_flag, p.err)) break;
-        const RawSlot& rs = sm.raw[s];
-        const uint4 dk = sm.dir[k][0], dv = sm.dir[k][1];
-        const int pos0 = (p.page_begin + sm.pages[k]) * DS;
-        // ---- stage out of the slot
-        uint4 kc0, kc1 = make_uint4(0, 0, 0, 0), vc0, vc1 = make_uint4(0, 0, 0, 0);
-        {
-          const uint8_t* kr = rs.codes + t * RBK + half * (RBK / 2);
-          const uint8_t* vr = rs.codes + DS * RBK + t * RBV + half * (RBV / 2);
-          kc0 = *reinterpret_cast<const uint4*>(kr);
-          if (BK == 4) kc1 = *reinterpret_cast<const uint4*>(kr + 16);
-          vc0 = *reinterpret_cast<const uint4*>(vr);
-          if (BV == 4) vc1 = *reinterpret_cast<const uint4*>(vr + 16);
-        }
-        const uint32_t nek = min(dk.z, (uint32_t)ENTCAP), nev = min(dv.z, (uint32_t)ENTCAP);
-        for (uint32_t e = lane; e < nek; e += 32) dq.ent[0][e] = rs.ent[0][e];
-        for (uint32_t e = lane; e < nev; e += 32) dq.ent[1][e] = rs.ent[1][e];
-        const bool vrows = pos0 < Tc && v_bulk(pos0);
-        if (vrows) {
+      // ---- K tile: per-channel LUT (lane = token t, half of the channels)
+      {
+        const uint8_t* rowp = ws.raw[st] + t * RBK + half * (RBK / 2);
+        // half 1's tables start 64 tables + 64 bytes later: its low address byte is 0x40
+        const uint32_t kbase = smem_u32(sm.klut) + (half ? (uint32_t)(64 * 2 * NLK + 64) : 0u);
+        const uint32_t low = half ? 0x40404040u : 0u;
+        if (BK == 4) {
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
+          const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-          for (int u = 0; u < DS * NLV / 32; ++u) dq.vlut[lane + 32 * u] = rs.vp[lane + 32 * u];
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.raw_empty[s]);
-
-        // ---- K: per-channel LUT (lane = token t, half of the channels)
-        {
-          uint16_t* tl = sm.tile[ts].k;
-          // half 1's tables start 64 tables + 64 bytes later: its low address byte is 0x40
-          const uint32_t kbase = smem_u32(sm.klut) + (half ? (uint32_t)(64 * 2 * NLK + 64) : 0u);
-          const uint32_t low = half ? 0x40404040u : 0u;
-          if (BK == 4) {
-            const uint32_t wv[8] = {kc0.x, kc0.y, kc0.z, kc0.w, kc1.x, kc1.y, kc1.z, kc1.w};
+          for (int w8 = 0; w8 < 8; ++w8) {
+            const uint4 o4 = lut8_nib<32>(wv[w8], low, kbase, 32u * 8u * (uint32_t)w8);
+            const int chunk = (8 * half + w8) ^ (t & 7);
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
+          }
+        } else {
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
 #pragma unroll
-            for (int w8 = 0; w8 < 8; ++w8) {
-              const uint4 o4 = lut8_nib<32>(wv[w8], low, kbase, 32u * 8u * (uint32_t)w8);
-              *reinterpret_cast<uint4*>(tl + t * DD + (((8 * half + w8) ^ (t & 7)) * 8)) = o4;
-            }
-          } else {
-            const uint32_t wv[4] = {kc0.x, kc0.y, kc0.z, kc0.w};
-#pragma unroll
-            for (int w4 = 0; w4 < 4; ++w4) {
-              uint4 o0, o1;
-              lut16_crumb<8>(wv[w4], low, kbase, 8u * 16u * (uint32_t)w4, o0, o1);
-              *reinterpret_cast<uint4*>(tl + t * DD + (((8 * half + 2 * w4) ^ (t & 7)) * 8)) = o0;
-              *reinterpret_cast<uint4*>(tl + t * DD + (((8 * half + 2 * w4 + 1) ^ (t & 7)) * 8)) = o1;
-            }
+          for (int w4 = 0; w4 < 4; ++w4) {
+            uint4 o0, o1;
+            lut16_crumb<8>(wv[w4], low, kbase, 8u * 16u * (uint32_t)w4, o0, o1);
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4) ^ (t & 7)) * 8)) = o0;
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4 + 1) ^ (t & 7)) * 8)) = o1;
           }
         }
-        // ---- V: per-token LUT (row min(pos, t_cal - 1))
-        {
-          uint16_t* tl = sm.tile[ts].v;
-          uint32_t vbase, vlow;
-          if (pos0 >= Tc) {
-            vbase = smem_u32(sm.vtail);  // one table for every token
-            vlow = 0u;
-          } else {
-            if (!vrows) {
-              uint16_t lv[DS * NLV / 32];
-#pragma unroll
-              for (int u = 0; u < DS * NLV / 32; ++u) {
-                const int i = lane + 32 * u;
-                const int r = i / NLV, c = i % NLV;
-                const int pr = min(pos0 + r, Tc - 1);
-                lv[u] = c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + pr) * p.sc.levels_v + c] : (uint16_t)0;
-              }
-#pragma unroll
-              for (int u = 0; u < DS * NLV / 32; ++u) dq.vlut[lane + 32 * u] = lv[u];
-              __syncwarp();
-            }
-            vbase = smem_u32(dq.vlut) + 2u * NLV * (uint32_t)t;  // token t's table
-            vlow = ((2u * NLV * (uint32_t)t) & 0xFFu) * 0x01010101u;
-          }
-          if (BV == 4) {
-            const uint32_t wv[8] = {vc0.x, vc0.y, vc0.z, vc0.w, vc1.x, vc1.y, vc1.z, vc1.w};
-#pragma unroll
-            for (int w8 = 0; w8 < 8; ++w8) {
-              const uint4 o4 = lut8_nib<0>(wv[w8], vlow, vbase, 0u);
-              *reinterpret_cast<uint4*>(tl + t * DD + (((8 * half + w8) ^ (t & 7)) * 8)) = o4;
-            }
-          } else {
-            const uint32_t wv[4] = {vc0.x, vc0.y, vc0.z, vc0.w};
-#pragma unroll
-            for (int w4 = 0; w4 < 4; ++w4) {
-              uint4 o0, o1;
-              lut16_crumb<0>(wv[w4], vlow, vbase, 0u, o0, o1);
-              *reinterpret_cast<uint4*>(tl + t * DD + (((8 * half + 2 * w4) ^ (t & 7)) * 8)) = o0;
-              *reinterpret_cast<uint4*>(tl + t * DD + (((8 * half + 2 * w4 + 1) ^ (t & 7)) * 8)) = o1;
-            }
-          }
-        }
-        __syncwarp();
-        // ---- outlier patches (entries past the staged ENTCAP come from the arena)
-        for (uint32_t e = lane; e < dk.z; e += 32) {
-          const uint32_t en = e < ENTCAP ? dq.ent[0][e] : p.pool.arena[dk.x + e];
-          const int et = (en >> 24) & 31, ed = (en >> 16) & 255;
-          if (et < DS && ed < DD) sm.tile[ts].k[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
-          else set_err(p.err, HX_DEV_ERR_BOUNDS);
-        }
-        for (uint32_t e = lane; e < dv.z; e += 32) {
-          const uint32_t en = e < ENTCAP ? dq.ent[1][e] : p.pool.arena[dv.x + e];
-          const int et = (en >> 24) & 31, ed = (en >> 16) & 255;
-          if (et < DS && ed < DD) sm.tile[ts].v[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
-          else set_err(p.err, HX_DEV_ERR_BOUNDS);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.tile_full[ts]);
       }
-    } else {
-      // ================= MMA warps: pages mw, mw + NMM, ...
-      for (int k = mw; k < cnt; k += NMM) {
-        if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-        const int K = done + k, ts = K % NTILE;
-        if (!warp_wait(&sm.tile_full[ts], (uint32_t)(K / NTILE) & 1u, abort_flag, p.err)) break;
-        const int j = sm.pages[k];
-        const int valid = seq_len - j * DS;  // tokens of this page inside the sequence
-        const uint16_t* kt = sm.tile[ts].k;
-        const uint16_t* vt = sm.tile[ts].v;
+      __syncwarp();
+      for (uint32_t e = lane; e < cntk; e += 32) {
+        uint32_t en = e < ENTCAP ? ws.ent[st][0][e] : p.pool.arena[offk + e];
+        int et = (en >> 24) & 31, ed = (en >> 16) & 255;
+        if (et < DS && ed < DD) ws.tile[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
+        else set_err(p.err, HX_DEV_ERR_BOUNDS);
+      }
+      __syncwarp();
 
-        // ---- S^T = K . Q^T  (16 tokens x 8 head columns), two accumulator chains
-        float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // ---- S^T = K . Q^T  (16 tokens x 8 head columns), two accumulator chains
+      float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          uint32_t a[4];
-          const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int chunk = (2 * ks + (lane >> 4)) ^ (r & 7);
-          ldmatrix_x4(a, kt + r * DD + chunk * 8);
-          if (ks & 1) mma_16816(sb, a, bq[ks][0], bq[ks][1]);
-          else mma_16816(sa, a, bq[ks][0], bq[ks][1]);
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a[4];
+        const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int chunk = (2 * ks + (lane >> 4)) ^ (r & 7);
+        ldmatrix_x4(a, ws.tile + r * DD + chunk * 8);
+        if (ks & 1) mma_16816(sb, a, bq[ks][0], bq[ks][1]);
+        else mma_16816(sa, a, bq[ks][0], bq[ks][1]);
+      }
+      // ---- online softmax (exp2 domain); rows = tokens g, g+8; cols = 2qd, 2qd+1
+      float x0 = (sa[0] + sb[0]) * p.scale_log2, x1 = (sa[1] + sb[1]) * p.scale_log2;
+      float x2 = (sa[2] + sb[2]) * p.scale_log2, x3 = (sa[3] + sb[3]) * p.scale_log2;
+      if (g >= valid) x0 = x1 = -INFINITY;
+      if (g + 8 >= valid) x2 = x3 = -INFINITY;
+      // the running max moves only when a score passes it by more than 2^8
+      const bool grow = fmaxf(x0, x2) > m0 + 8.0f || fmaxf(x1, x3) > m1 + 8.0f;
+      if (__any_sync(0xffffffffu, grow)) {
+        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+        for (int sft = 4; sft <= 16; sft <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sft));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sft));
         }
-        // ---- online softmax (exp2 domain); rows = tokens g, g+8; cols = 2qd, 2qd+1
-        float x0 = (sa[0] + sb[0]) * p.scale_log2, x1 = (sa[1] + sb[1]) * p.scale_log2;
-        float x2 = (sa[2] + sb[2]) * p.scale_log2, x3 = (sa[3] + sb[3]) * p.scale_log2;
-        if (g >= valid) x0 = x1 = -INFINITY;
-        if (g + 8 >= valid) x2 = x3 = -INFINITY;
-        // the running max moves only when a score passes it by more than 2^8
-        const bool grow = fmaxf(x0, x2) > m0 + 8.0f || fmaxf(x1, x3) > m1 + 8.0f;
-        if (__any_sync(0xffffffffu, grow)) {
-          float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-#pragma unroll
-          for (int s = 4; s <= 16; s <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, s));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, s));
-          }
-          const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-          const float al0 = m0 == -INFINITY ? 0.0f : exp2f(m0 - mn0);
-          const float al1 = m1 == -INFINITY ? 0.0f : exp2f(m1 - mn1);
-          l0 *= al0;
-          l1 *= al1;
-#pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            oacc[mt][0] *= al0;
-            oacc[mt][1] *= al1;
-            oacc[mt][2] *= al0;
-            oacc[mt][3] *= al1;
-          }
-          m0 = mn0;
-          m1 = mn1;
-        }
-        const float bs0 = m0 == -INFINITY ? 0.0f : m0, bs1 = m1 == -INFINITY ? 0.0f : m1;
-        const float p0 = exp2f(x0 - bs0), p1 = exp2f(x1 - bs1), p2 = exp2f(x2 - bs0), p3 = exp2f(x3 - bs1);
-        l0 += p0 + p2;
-        l1 += p1 + p3;
-        // P^T as the B operand (k = token, n = head column): hi and lo halves
-        const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
-        const __half h2 = __float2half_rn(p2), h3 = __float2half_rn(p3);
-        const uint32_t phi_top = pack_u16x2(__half_as_ushort(h0), __half_as_ushort(h1));
-        const uint32_t phi_bot = pack_u16x2(__half_as_ushort(h2), __half_as_ushort(h3));
-        const uint32_t plo_top = pack_half2(p0 - __half2float(h0), p1 - __half2float(h1));
-        const uint32_t plo_bot = pack_half2(p2 - __half2float(h2), p3 - __half2float(h3));
-        const uint32_t bh0 = movmatrix_trans(phi_top), bh1 = movmatrix_trans(phi_bot);
-        const uint32_t bl0 = movmatrix_trans(plo_top), bl1 = movmatrix_trans(plo_bot);
-        // ---- O^T += V^T . P^T  (128 channels x 8 head columns)
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float al0 = m0 == -INFINITY ? 0.0f : exp2f(m0 - mn0);
+        const float al1 = m1 == -INFINITY ? 0.0f : exp2f(m1 - mn1);
+        l0 *= al0;
+        l1 *= al1;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
-          uint32_t a[4];
-          const int r = (lane & 7) + ((lane >> 4) & 1) * 8;
-          const int chunk = (2 * mt + ((lane >> 3) & 1)) ^ (r & 7);
-          ldmatrix_x4_trans(a, vt + r * DD + chunk * 8);
-          mma_16816(oacc[mt], a, bh0, bh1);
-          mma_16816(oacc[mt], a, bl0, bl1);
+          oacc[mt][0] *= al0;
+          oacc[mt][1] *= al1;
+          oacc[mt][2] *= al0;
+          oacc[mt][3] *= al1;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.tile_empty[ts]);
+        m0 = mn0;
+        m1 = mn1;
       }
+      const float bs0 = m0 == -INFINITY ? 0.0f : m0, bs1 = m1 == -INFINITY ? 0.0f : m1;
+      const float p0 = exp2f(x0 - bs0), p1 = exp2f(x1 - bs1), p2 = exp2f(x2 - bs0), p3 = exp2f(x3 - bs1);
+      l0 += p0 + p2;
+      l1 += p1 + p3;
+      // P^T as the B operand (k = token, n = head column): hi and lo halves
+      const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
+      const __half h2 = __float2half_rn(p2), h3 = __float2half_rn(p3);
+      const uint32_t phi_top = pack_u16x2(__half_as_ushort(h0), __half_as_ushort(h1));
+      const uint32_t phi_bot = pack_u16x2(__half_as_ushort(h2), __half_as_ushort(h3));
+      const uint32_t plo_top = pack_half2(p0 - __half2float(h0), p1 - __half2float(h1));
+      const uint32_t plo_bot = pack_half2(p2 - __half2float(h2), p3 - __half2float(h3));
+      const uint32_t bh0 = movmatrix_trans(phi_top), bh1 = movmatrix_trans(phi_bot);
+      const uint32_t bl0 = movmatrix_trans(plo_top), bl1 = movmatrix_trans(plo_bot);
+
+      // ---- V tile: per-token LUT (row min(pos, t_cal - 1))
+      uint32_t vbase, vlow;
+      if (pos0 >= Tc) {
+        vbase = smem_u32(sm.vtail);  // one table for every token
+        vlow = 0u;
+      } else {
+        if (v_bulk(pos0)) {
+          vbase = smem_u32(ws.vp[st]);
+        } else {
+          uint16_t lv[DS * NLV / 32];
+#pragma unroll
+          for (int u = 0; u < DS * NLV / 32; ++u) {
+            const int i = lane + 32 * u;
+            const int r = i / NLV, c = i % NLV;
+            const int pr = min(pos0 + r, Tc - 1);
+            lv[u] = c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + pr) * p.sc.levels_v + c] : (uint16_t)0;
+          }
+#pragma unroll
+          for (int u = 0; u < DS * NLV / 32; ++u) ws.vlut[lane + 32 * u] = lv[u];
+          __syncwarp();
+          vbase = smem_u32(ws.vlut);
+        }
+        vbase += 2u * NLV * (uint32_t)t;  // token t's table
+        vlow = ((2u * NLV * (uint32_t)t) & 0xFFu) * 0x01010101u;
+      }
+      {
+        const uint8_t* rowp = ws.raw[st] + DS * RBK + t * RBV + half * (RBV / 2);
+        if (BV == 4) {
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
+          const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+          for (int w8 = 0; w8 < 8; ++w8) {
+            const uint4 o4 = lut8_nib<0>(wv[w8], vlow, vbase, 0u);
+            const int chunk = (8 * half + w8) ^ (t & 7);
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
+          }
+        } else {
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            uint4 o0, o1;
+            lut16_crumb<0>(wv[w4], vlow, vbase, 0u, o0, o1);
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4) ^ (t & 7)) * 8)) = o0;
+            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4 + 1) ^ (t & 7)) * 8)) = o1;
+          }
+        }
+      }
+      __syncwarp();
+      for (uint32_t e = lane; e < cntv; e += 32) {
+        uint32_t en = e < ENTCAP ? ws.ent[st][1][e] : p.pool.arena[offv + e];
+        int et = (en >> 24) & 31, ed = (en >> 16) & 255;
+        if (et < DS && ed < DD) ws.tile[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
+        else set_err(p.err, HX_DEV_ERR_BOUNDS);
+      }
+      __syncwarp();
+
+      // ---- O^T += V^T . P^T  (128 channels x 8 head columns)
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        uint32_t a[4];
+        const int r = (lane & 7) + ((lane >> 4) & 1) * 8;
+        const int chunk = (2 * mt + ((lane >> 3) & 1)) ^ (r & 7);
+        ldmatrix_x4_trans(a, ws.tile + r * DD + chunk * 8);
+        mma_16816(oacc[mt], a, bh0, bh1);
+        mma_16816(oacc[mt], a, bl0, bl1);
+      }
+      __syncwarp();
+    }
+    if (timed_out) {
+      // give copies still in flight one more bounded wait before the buffers
+      // are reused, then stop this warp's work
+      for (int st = 0; st < NSTAGE; ++st)
+        if ((inflight >> st) & 1u && mbar_wait(&ws.bar[st], (phase >> st) & 1u)) {
+          phase ^= 1u << st;
+          inflight &= ~(1u << st);
+        }
     }
     __syncthreads();
-    done += cnt;
   }
 
-  // ---- MMA warps -> CTA partial (smem reuses the tile ring)
-  float* wO = reinterpret_cast<float*>(sm.tile);  // [NMM][8][128] floats = 32 KB
-  if (is_mma) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 4);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 8);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 16);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 8);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
-    float* myO = wO + mw * 8 * DD;
+  // ---- warp -> CTA merge (smem reuses the stage buffers)
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 4);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 8);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 16);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 8);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
+  float* wO = reinterpret_cast<float*>(ws.raw);     // [8][128] floats = 4 KB
+  float* wml = reinterpret_cast<float*>(ws.vlut);   // m[8], l[8]
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      const int d = 16 * mt + g;
-      myO[(2 * qd) * DD + d] = oacc[mt][0];
-      myO[(2 * qd + 1) * DD + d] = oacc[mt][1];
-      myO[(2 * qd) * DD + d + 8] = oacc[mt][2];
-      myO[(2 * qd + 1) * DD + d + 8] = oacc[mt][3];
-    }
-    if (g == 0) {
-      sm.wml[mw][2 * qd] = m0;
-      sm.wml[mw][2 * qd + 1] = m1;
-      sm.wml[mw][8 + 2 * qd] = l0;
-      sm.wml[mw][8 + 2 * qd + 1] = l1;
-    }
+  for (int mt = 0; mt < 8; ++mt) {
+    const int d = 16 * mt + g;
+    wO[(2 * qd) * DD + d] = oacc[mt][0];
+    wO[(2 * qd + 1) * DD + d] = oacc[mt][1];
+    wO[(2 * qd) * DD + d + 8] = oacc[mt][2];
+    wO[(2 * qd + 1) * DD + d + 8] = oacc[mt][3];
+  }
+  if (g == 0) {
+    wml[2 * qd] = m0;
+    wml[2 * qd + 1] = m1;
+    wml[8 + 2 * qd] = l0;
+    wml[8 + 2 * qd + 1] = l1;
   }
   __syncthreads();
+  // per-column warp maxima and sums, then (column, channel) sums over the warps
   if (tid < G) {
     const int c = tid;
     float M = -INFINITY;
-    for (int w = 0; w < NMM; ++w) M = fmaxf(M, sm.wml[w][c]);
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, reinterpret_cast<float*>(sm.w[w].vlut)[c]);
     const float base = M == -INFINITY ? 0.0f : M;
     float L = 0.0f;
-    for (int w = 0; w < NMM; ++w) L += exp2f(sm.wml[w][c] - base) * sm.wml[w][8 + c];
+    for (int w = 0; w < NW; ++w) {
+      const float* ml = reinterpret_cast<float*>(sm.w[w].vlut);
+      L += exp2f(ml[c] - base) * ml[8 + c];
+    }
     sm.colM[c] = M;
     sm.colL[c] = L;
   }
@@ -640,8 +537,10 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
     const float M = sm.colM[c];
     const float base = M == -INFINITY ? 0.0f : M;
     float O = 0.0f;
-#pragma unroll
-    for (int w = 0; w < NMM; ++w) O += exp2f(sm.wml[w][c] - base) * wO[(w * 8 + c) * DD + d];
+    for (int w = 0; w < NW; ++w) {
+      const float sc = exp2f(reinterpret_cast<float*>(sm.w[w].vlut)[c] - base);
+      O += sc * reinterpret_cast<float*>(sm.w[w].raw)[c * DD + d];
+    }
     mypart[c * DD + d] = O;
   }
   if (tid < G) {
@@ -656,10 +555,11 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   __threadfence();
 
   // ---- last CTA of (b, h): merge the splits
+  __syncthreads();  // every thread is past its reads of the warp buffers
   const float* parts = p.part + (int64_t)bh * p.n_splits * PSZ;
-  float* wts = reinterpret_cast<float*>(sm.raw);  // [n_splits][8] weights (raw + tile are contiguous)
-  float* sMv = wts + MAXSPLIT * 8;                // [n_splits][8] split maxima
-  float* sLv = sMv + MAXSPLIT * 8;                // [n_splits][8] split sums
+  float* wts = reinterpret_cast<float*>(sm.w);  // [n_splits][8] weights (in the warp buffers)
+  float* sMv = wts + MAXSPLIT * 8;               // [n_splits][8] split maxima
+  float* sLv = sMv + MAXSPLIT * 8;               // [n_splits][8] split sums
   for (int i = tid; i < p.n_splits * 8; i += NT) {
     const int s = i >> 3, c = i & 7;
     sMv[i] = __ldcg(parts + (int64_t)s * PSZ + 8 * DD + c);
