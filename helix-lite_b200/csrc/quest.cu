@@ -236,14 +236,19 @@ __global__ void __launch_bounds__(256) quest_scores_d128_kernel(const uint16_t* 
 }
 
 // TMA-staged scores for fp16 stats with D = 128 whose min and max rows are
-// adjacent (kmax == kmin + 128, the pool layout). Persistent: each warp takes
-// batches of 32 pages of one (b, h); lane l bulk-copies page l's 512-byte
-// {min, max} record into a 2-stage smem buffer, so 16 KB per warp are in
-// flight; the arithmetic is the pinned order of quest_scores_d128_kernel.
-constexpr int kQW = 4;      // warps per block
-constexpr int kQStages = 3; // batches in smem per warp (2 in flight while one is scored)
+// adjacent (kmax == kmin + 128, the pool layout). Persistent, 16 warps per
+// SM so the scoring arithmetic hides its latencies: each warp takes batches
+// of 8 pages of one (b, h); a page's 512-byte {min, max} record lands in a
+// 3-stage smem ring by bulk copy (one copy per run of adjacent records). The
+// arithmetic is the pinned order of quest_scores_d128_kernel: lane l scores
+// channels 4l .. 4l+3 of every page, then the pages are summed across lanes
+// in the butterfly order (xor 16, 8, 4, 2, 1), the first three stages
+// transposed so that lane l ends with page l / 4.
+constexpr int kQW = 16;      // warps per block
+constexpr int kQPB = 8;      // pages per batch
+constexpr int kQStages = 3;  // batches in smem per warp (2 in flight while one is scored)
 struct __align__(128) QuestSmem {
-  uint16_t rec[kQW][kQStages][32][256];  // [warp][stage][page][min 128 | max 128]
+  uint16_t rec[kQW][kQStages][kQPB][256];  // [warp][stage][page][min 128 | max 128]
   uint64_t bar[kQW][kQStages];
   float qp[kQW][128], qn[kQW][128];
 };
@@ -256,7 +261,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   extern __shared__ __align__(128) uint8_t smem_raw[];
   QuestSmem& sm = *reinterpret_cast<QuestSmem*>(smem_raw);
   const int lane = lane_id(), warp = threadIdx.x >> 5;
-  const int nb = (max_pages + 31) / 32;  // batches per (b, h)
+  const int nb = (max_pages + kQPB - 1) / kQPB;  // batches per (b, h)
   const int64_t total = (int64_t)B * H * nb;
   const int64_t gw = (int64_t)blockIdx.x * kQW + warp, nw = (int64_t)gridDim.x * kQW;
   if (lane == 0) {
@@ -265,23 +270,29 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   }
   __syncthreads();
 
-  // Batch k of this warp is global batch gw + k * nw. For a batch: its pages
-  // count (lanes < cnt hold a page) and lane's physical page.
+  // A warp takes a contiguous run of batches (so it rarely changes (b, h)):
+  // batch k of this warp is global batch g0 + k. For a batch: its pages count
+  // (lanes < cnt hold a page), the sequence's sinks, lane's physical page.
   struct Bat {
-    int bh, j0, cnt;
+    int bh, j0, cnt, sinks;
     int64_t phys;
   };
   auto plan = [&](int64_t it) -> Bat {
     Bat r;
     r.bh = (int)(it / nb);
-    r.j0 = (int)(it % nb) * 32;
+    r.j0 = (int)(it % nb) * kQPB;
     const int b = r.bh / H;
     const int n = min((seq_lens[b] + S - 1) / S, max_pages);
-    r.cnt = max(0, min(32, n - r.j0));
+    r.cnt = max(0, min(kQPB, n - r.j0));
+    r.sinks = min(max(sinks_req, 0), n);
     const int j = r.j0 + lane;
     r.phys = (lane < r.cnt) ? (bt ? (int64_t)bt[(int64_t)b * bt_stride + j] : (int64_t)j) : 0;
     return r;
   };
+  // Pages whose records are adjacent in memory (consecutive physical pages,
+  // records page_stride == 256 elements apart) go as one copy per run: the
+  // copy engine's cost is per copy, not per byte.
+  const bool adjacent = page_stride == 256;
   auto issue = [&](const Bat& bb, int st) {
     if (bb.cnt <= 0) return;
     if (lane == 0) {
@@ -289,55 +300,63 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
       mbar_arrive_expect_tx(&sm.bar[warp][st], (uint32_t)bb.cnt * 512u);
     }
     __syncwarp();
-    if (lane < bb.cnt)
-      bulk_g2s(sm.rec[warp][st][lane], kmin + bb.phys * page_stride + (int64_t)(bb.bh % H) * head_stride, 512u,
-               &sm.bar[warp][st]);
+    const int64_t prev = __shfl_up_sync(0xffffffffu, bb.phys, 1);
+    const bool start = lane < bb.cnt && (lane == 0 || !adjacent || bb.phys != prev + 1);
+    const uint32_t starts = __ballot_sync(0xffffffffu, start);
+    if (start) {
+      const uint32_t later = starts & ~((2u << lane) - 1u);  // run starts after this lane
+      const int end = later ? __ffs(later) - 1 : bb.cnt;
+      bulk_g2s(sm.rec[warp][st][lane], kmin + bb.phys * page_stride + (int64_t)(bb.bh % H) * head_stride,
+               512u * (uint32_t)(end - lane), &sm.bar[warp][st]);
+    }
   };
 
-  const int nk = gw < total ? (int)((total - 1 - gw) / nw) + 1 : 0;
-  Bat p0 = {0, 0, 0, 0}, p1 = {0, 0, 0, 0}, p2 = {0, 0, 0, 0};
-  if (nk > 0) p0 = plan(gw);
-  if (nk > 1) p1 = plan(gw + nw);
-  if (nk > 2) p2 = plan(gw + 2 * nw);
+  const int64_t per = (total + nw - 1) / nw;
+  const int64_t g0 = gw * per;
+  const int nk = (int)max((int64_t)0, min(per, total - g0));
+  Bat p0 = {0, 0, 0, 0, 0}, p1 = {0, 0, 0, 0, 0}, p2 = {0, 0, 0, 0, 0};
+  if (nk > 0) p0 = plan(g0);
+  if (nk > 1) p1 = plan(g0 + 1);
+  if (nk > 2) p2 = plan(g0 + 2);
   issue(p0, 0);
   issue(p1, 1 % kQStages);
   int cur_bh = -1;
   uint32_t phase = 0;
   bool dead = false;
+  float qp[4], qn[4];
   for (int k = 0; k < nk; ++k) {
     const int st = k % kQStages;
     // keep two batches in flight: issue k + 2 now, plan k + 3 (its block-table
     // reads overlap this batch's work)
     if (k + 2 < nk) issue(p2, (k + 2) % kQStages);
-    Bat p3 = {0, 0, 0, 0};
-    if (k + 3 < nk) p3 = plan(gw + (int64_t)(k + 3) * nw);
+    Bat p3 = {0, 0, 0, 0, 0};
+    if (k + 3 < nk) p3 = plan(g0 + k + 3);
     const Bat cb = p0;
     if (cb.cnt > 0) {
+      const int b = cb.bh / H, h = cb.bh % H;
+      if (cb.bh != cur_bh) {
+        for (int d = lane; d < 128; d += 32) {
+          float a, c;
+          group_terms(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, 128, mode, d, a, c);
+          sm.qp[warp][d] = a;
+          sm.qn[warp][d] = c;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          qp[v] = sm.qp[warp][4 * lane + v];
+          qn[v] = sm.qn[warp][4 * lane + v];
+        }
+        cur_bh = cb.bh;
+      }
       if (!dead && !mbar_wait(&sm.bar[warp][st], (phase >> st) & 1u)) {
         dead = true;
         if (lane == 0) set_err(err, HX_DEV_ERR_TIMEOUT);
       }
       phase ^= 1u << st;
-      const int b = cb.bh / H, h = cb.bh % H;
-      if (cb.bh != cur_bh) {
-        for (int d = lane; d < 128; d += 32) {
-          float qp, qn;
-          group_terms(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, 128, mode, d, qp, qn);
-          sm.qp[warp][d] = qp;
-          sm.qn[warp][d] = qn;
-        }
-        __syncwarp();
-        cur_bh = cb.bh;
-      }
-      float qp[4], qn[4];
+      float part[kQPB];
 #pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        qp[v] = sm.qp[warp][4 * lane + v];
-        qn[v] = sm.qn[warp][4 * lane + v];
-      }
-      float part[32];
-#pragma unroll
-      for (int u = 0; u < 32; ++u) {
+      for (int u = 0; u < kQPB; ++u) {
         const uint2 c = *reinterpret_cast<const uint2*>(&sm.rec[warp][st][u][4 * lane]);
         const uint2 a = *reinterpret_cast<const uint2*>(&sm.rec[warp][st][u][128 + 4 * lane]);
         const uint16_t xa[4] = {(uint16_t)(a.x & 0xffff), (uint16_t)(a.x >> 16), (uint16_t)(a.y & 0xffff),
@@ -352,22 +371,24 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
         }
         part[u] = acc;
       }
+      // stages 16, 8, 4 transposed (8 -> 1 values a lane), then 2, 1 plain
 #pragma unroll
-      for (int m = 16; m >= 1; m >>= 1) {
+      for (int m = 16, half = kQPB / 2; m >= 4; m >>= 1, half >>= 1) {
         const bool upper = (lane & m) != 0;
 #pragma unroll
-        for (int i = 0; i < m; ++i) {
-          const float send = upper ? part[i] : part[i + m];
-          const float keep = upper ? part[i + m] : part[i];
+        for (int i = 0; i < half; ++i) {
+          const float send = upper ? part[i] : part[i + half];
+          const float keep = upper ? part[i + half] : part[i];
           part[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
         }
       }
-      const int j = cb.j0 + lane;
-      if (lane < cb.cnt) {
-        const int n = min((seq_lens[b] + S - 1) / S, max_pages);
-        const int sinks = min(max(sinks_req, 0), n);
+      part[0] = __fadd_rn(part[0], __shfl_xor_sync(0xffffffffu, part[0], 2));
+      part[0] = __fadd_rn(part[0], __shfl_xor_sync(0xffffffffu, part[0], 1));
+      const int u = lane >> 2, j = cb.j0 + u;
+      if ((lane & 3) == 0 && u < cb.cnt) {
         scores[(int64_t)cb.bh * max_pages + j] = part[0];
-        if (hist && j >= sinks) atomicAdd(&hist[(int64_t)cb.bh * 2 * kBins + (order_key(part[0]) >> 20)], 1u);
+        if (hist && j >= cb.sinks)
+          atomicAdd(&hist[(int64_t)cb.bh * 2 * kBins + (order_key(part[0]) >> 20)], 1u);
       }
     }
     __syncwarp();
@@ -468,7 +489,9 @@ HX_DEVINL int find_boundary(const uint32_t* s_hist, uint32_t need, uint32_t& abo
 // Select the r-th largest among `cnt` unique 64-bit keys, counting only keys
 // whose bits above `shift` equal `prefix`, by 8-bit digit passes from bit
 // shift-1 down. Returns the threshold T with
-// exactly r keys >= T (among the candidates). blockDim == 256.
+// exactly r keys >= T (among the candidates). blockDim == 256. kGlobal: the
+// keys are in global memory written by other blocks (read through L2).
+template <bool kGlobal>
 HX_DEVINL uint64_t radix_select(const uint64_t* cand, uint32_t cnt, uint32_t r, uint64_t prefix, int shift,
                                 uint32_t* s_h, uint32_t* s_warp, int* s_res) {
   uint64_t mask = ~((1ull << shift) - 1ull);
@@ -483,7 +506,7 @@ HX_DEVINL uint64_t radix_select(const uint64_t* cand, uint32_t cnt, uint32_t r, 
 #pragma unroll
       for (int u = 0; u < 4; ++u) {  // written by other blocks: read through L2
         const uint32_t i = i0 + u * blockDim.x + threadIdx.x;
-        key[u] = i < cnt ? __ldcg(cand + i) : ~prefix;
+        key[u] = i < cnt ? (kGlobal ? __ldcg(cand + i) : cand[i]) : ~prefix;
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u)
@@ -504,17 +527,32 @@ HX_DEVINL uint64_t radix_select(const uint64_t* cand, uint32_t cnt, uint32_t r, 
   return prefix;
 }
 
+// Copy a 4096-bin histogram to smem with all of a thread's loads in flight
+// (blockDim == 256: four 16-byte loads each), through L2: other blocks wrote it.
+HX_DEVINL void load_hist(uint32_t* s_hist, const uint32_t* g) {
+  uint4 v[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const uint4*>(g) + u * 256 + threadIdx.x);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) reinterpret_cast<uint4*>(s_hist)[u * 256 + threadIdx.x] = v[u];
+}
+
 // hist layout per (b, h): [level 1: 4096 bins of key32 >> 20 | level 2: 4096
-// bins of key32 bits 19..8 among the level-1 boundary bin's pages].
+// bins of key32 bits 19..8 among the level-1 boundary bin's pages]. The last
+// block gathers the keys of the level-2 boundary bin (a handful) into smem
+// and finishes the radix select there.
+constexpr int kCandSmem = 1024;
 __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __restrict__ scores, int H,
                                                               const int32_t* __restrict__ seq_lens, int S,
                                                               int max_pages, int sinks_req, int k_fixed, int fnum,
                                                               int fden, uint32_t* hist, uint64_t* cand,
                                                               uint32_t* counters, uint64_t* thresh, uint32_t* err) {
-  __shared__ uint32_t s_hist[kBins];
+  __shared__ __align__(16) uint32_t s_hist[kBins];
   __shared__ uint32_t s_warp[8];
   __shared__ int s_res[4];
   __shared__ uint32_t s_h2[256];
+  __shared__ uint64_t s_cand[kCandSmem];
+  __shared__ uint32_t s_nc;
   __shared__ int s_last;
   const int bh = blockIdx.y;
   const int b = bh / H;
@@ -531,16 +569,19 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
   bool full_bin = false;
   const bool trivial = (pl.k_eff == 0) || (pl.k_eff >= n_ns);
   if (!trivial) {
-    for (int i = threadIdx.x; i < kBins; i += blockDim.x) s_hist[i] = hist_bh[i];
+    load_hist(s_hist, hist_bh);
     __syncthreads();
     bstar = find_boundary(s_hist, (uint32_t)pl.k_eff, above, s_warp, s_res);
     r = (uint32_t)pl.k_eff - above;
     full_bin = bstar >= 0 && s_hist[bstar] == r;
     if (bstar >= 0 && !full_bin) {
-      // this block's candidates of bin b*, with their level-2 histogram
+      // this block's candidates of bin b*, with their level-2 histogram:
+      // staged in smem, then one global reservation for the block
       const int per = (n_ns + C - 1) / C;
       const int a = pl.sinks + blockIdx.x * per;
       const int e = min(a + per, pl.n);
+      if (threadIdx.x == 0) s_nc = 0;
+      __syncthreads();
       for (int base = a; base < e; base += 4 * blockDim.x) {
         float v[4];
 #pragma unroll
@@ -551,22 +592,25 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int j = base + u * blockDim.x + threadIdx.x;
-          bool hit = false;
-          uint32_t k32 = 0;
           if (j < e) {
-            k32 = order_key(v[u]);
-            hit = (int)(k32 >> 20) == bstar;
-          }
-          const uint32_t m = __ballot_sync(0xffffffffu, hit);
-          uint32_t pos = 0;
-          if (lane_id() == 0 && m) pos = atomicAdd(&ctr[0], (uint32_t)__popc(m));
-          pos = __shfl_sync(0xffffffffu, pos, 0);
-          if (hit) {
-            cand_bh[pos + __popc(m & ((1u << lane_id()) - 1))] = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
-            atomicAdd(&hist2_bh[(k32 >> 8) & (kBins - 1)], 1u);
+            const uint32_t k32 = order_key(v[u]);
+            if ((int)(k32 >> 20) == bstar) {
+              const uint64_t key = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
+              const uint32_t at = atomicAdd(&s_nc, 1u);
+              if (at < (uint32_t)kCandSmem) s_cand[at] = key;
+              else cand_bh[atomicAdd(&ctr[0], 1u)] = key;  // a slice past kCandSmem hits (long sequences)
+              atomicAdd(&hist2_bh[(k32 >> 8) & (kBins - 1)], 1u);
+            }
           }
         }
       }
+      __syncthreads();
+      const uint32_t nloc = min(s_nc, (uint32_t)kCandSmem);
+      if (threadIdx.x == 0) s_res[0] = (int)atomicAdd(&ctr[0], nloc);
+      __syncthreads();
+      const uint32_t gbase = (uint32_t)s_res[0];
+      for (uint32_t i = threadIdx.x; i < nloc; i += blockDim.x) cand_bh[gbase + i] = s_cand[i];
+      __syncthreads();
     }
   }
   __threadfence();
@@ -588,7 +632,7 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
     T = (uint64_t)bstar << 52;
   } else {
     const uint32_t cnt = *((volatile uint32_t*)&ctr[0]);
-    for (int i = threadIdx.x; i < kBins; i += blockDim.x) s_hist[i] = __ldcg(&hist2_bh[i]);
+    load_hist(s_hist, hist2_bh);
     __syncthreads();
     uint32_t above2;
     const int b2 = find_boundary(s_hist, r, above2, s_warp, s_res);
@@ -598,8 +642,48 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
     } else {
       const uint32_t r2 = r - above2;
       const uint64_t pre = ((uint64_t)bstar << 52) | ((uint64_t)b2 << 40);
-      if (s_hist[b2] == r2) T = pre;
-      else T = radix_select(cand_bh, cnt, r2, pre, 40, s_h2, s_warp, s_res);
+      if (s_hist[b2] == r2) {
+        T = pre;
+      } else {
+        // gather the level-2 boundary bin's keys into smem and select there
+        if (threadIdx.x == 0) s_nc = 0;
+        __syncthreads();
+        for (uint32_t i0 = 0; i0 < cnt; i0 += 16 * blockDim.x) {
+          uint64_t key[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const uint32_t i = i0 + u * blockDim.x + threadIdx.x;
+            key[u] = i < cnt ? __ldcg(cand_bh + i) : 0ull;
+          }
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            if (i0 + u * blockDim.x + threadIdx.x < cnt && (key[u] >> 40) == (pre >> 40)) {
+              const uint32_t at = atomicAdd(&s_nc, 1u);
+              if (at < (uint32_t)kCandSmem) s_cand[at] = key[u];
+            }
+          }
+        }
+        __syncthreads();
+        const uint32_t nc = s_nc;
+        if (nc <= blockDim.x) {
+          // a handful of keys: key i is T when exactly r2 - 1 keys beat it
+          if (threadIdx.x == 0) s_res[0] = -1;
+          __syncthreads();
+          if (threadIdx.x < nc) {
+            const uint64_t mine = s_cand[threadIdx.x];
+            uint32_t beat = 0;
+            for (uint32_t i = 0; i < nc; ++i) beat += s_cand[i] > mine;
+            if (beat + 1 == r2) s_res[0] = (int)threadIdx.x;
+          }
+          __syncthreads();
+          const int w = s_res[0];
+          T = w >= 0 ? s_cand[w] : pre;
+          if (w < 0 && threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
+        } else {
+          T = nc <= (uint32_t)kCandSmem ? radix_select<false>(s_cand, nc, r2, pre, 40, s_h2, s_warp, s_res)
+                                        : radix_select<true>(cand_bh, cnt, r2, pre, 40, s_h2, s_warp, s_res);
+        }
+      }
     }
   }
   if (threadIdx.x == 0) {
@@ -819,7 +903,7 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
         return HX_ERR_LAUNCH;
       attr[dev] = true;
     }
-    int64_t batches = (int64_t)B * H * ((max_pages + 31) / 32);
+    int64_t batches = (int64_t)B * H * ((max_pages + kQPB - 1) / kQPB);
     int64_t want = (batches + kQW - 1) / kQW;
     int grid = (int)(want < 148 ? want : 148);
     quest_scores_tma_kernel<<<grid, kQW * 32, sizeof(QuestSmem), s>>>(
