@@ -1,0 +1,106 @@
+"""The vLLM hooks end to end on the GPU, with a stand-in FlashAttentionImpl
+(no vLLM engine): the compact-pool hook's cache update + decode against the
+oracle's selection and attention, and the quantise-dequantise hook against
+the oracle's reconstruction."""
+from __future__ import annotations
+
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import np16, oracle_scales
+from oracle import attention as oatt
+from oracle import quest as oq
+from oracle.pool import OraclePool
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+class FakeImpl:
+    def __init__(self, scale):
+        self.scale, self.sliding_window, self.alibi_slopes = scale, (-1, -1), None
+        self.logits_soft_cap, self.sinks, self.sent = 0, None, []
+
+    def forward(self, layer, query, key, value, kv_cache, attn_metadata, output,
+                output_scale=None, output_block_scale=None):
+        self.sent.append((key.clone(), value.clone()))
+        return output
+
+    def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping):
+        pass
+
+
+class FakeBackend:
+    get_impl_cls = staticmethod(lambda: FakeImpl)
+
+
+def test_compact_hook_decode_matches_oracle():
+    from kvquant import compact_backend as cb
+    from kvquant.synthetic import NUQ4, make_kv, make_scales
+    H, D, S, n, G = 4, 128, 16, 3000, 7
+    sc = make_scales([NUQ4], H, D, t_cal=1024, seed=70)
+    backend = type("B", (FakeBackend,), {})
+    n_pages = -(-n // S)
+    cb.install_compact_backend("", num_layers=1, num_blocks=n_pages, block_size=S, num_kv_heads=H, head_size=D,
+                               device="cuda", top_k_blocks_decode=n_pages // 4, sink_blocks=4, gqa="sum",
+                               scales=sc, backend_cls=backend, impl_cls=FakeImpl)
+    impl = backend.get_impl_cls()(scale=D ** -0.5)
+    layer = types.SimpleNamespace(layer_name="model.layers.0.self_attn.attn")
+    K, V = make_kv(n, H, D, seed=71, chan_seed=70)
+    slots = torch.arange(n, device="cuda")
+    for a in range(0, n, 1000):                       # a prefill in chunks, as vLLM updates the cache
+        impl.do_kv_cache_update(layer, K[a:a + 1000], V[a:a + 1000], None, slots[a:a + 1000])
+    cb.pool().check()
+    g = torch.Generator(device="cuda").manual_seed(72)
+    q = torch.randn((1, H * G, D), generator=g, device="cuda").to(torch.float16)
+    meta = types.SimpleNamespace(max_query_len=1, num_actual_tokens=1, causal=True,
+                                 block_table=torch.arange(n_pages, dtype=torch.int32, device="cuda").unsqueeze(0),
+                                 seq_lens=torch.tensor([n], dtype=torch.int32, device="cuda"))
+    out = torch.zeros((1, H * G, D), dtype=torch.float16, device="cuda")
+    impl.forward(layer, q, K[:1], V[:1], None, meta, out)
+    cb.pool().check()
+    assert not impl.sent                              # served by the fused path, not FlashAttention
+    orc = OraclePool(1, n_pages, S, H, D, oracle_scales(sc))
+    orc.write_kv(0, np16(K), np16(V), np16(slots), np16(slots))
+    kmin = orc.stats[0][:, :n_pages, 0].transpose(1, 0, 2)
+    kmax = orc.stats[0][:, :n_pages, 1].transpose(1, 0, 2)
+    qp, qn = oq.group_terms(np16(q[0]), G, "sum")
+    ref = oq.page_scores(qp, qn, kmin, kmax)
+    pages = [oq.select_pages(ref[:, h], n_pages // 4, 4) for h in range(H)]
+    Kd, Vd = orc.dequant_sequence(0, np.arange(n_pages), n)
+    o, _ = oatt.decode_attention(np16(q[0]).astype(np.float64), Kd, Vd,
+                                 oatt.page_mask_to_token_mask(pages, n, S))
+    # the hook writes vLLM's fp16 output: TOL plus half an fp16 ulp of the value
+    err = np.abs(np16(out[0]).astype(np.float64) - o)
+    assert (err <= TOL + np.abs(o) * 2.0 ** -11).all(), err.max()
+
+
+def test_quantise_dequantise_hook_matches_oracle():
+    from kvquant import vllm_backend as vb
+    from kvquant.synthetic import NUQ4, make_kv, make_scales
+    from oracle.pool import quantize_k_rows, quantize_v_rows
+    H, D = 4, 128
+    sc = make_scales([NUQ4, NUQ4], H, D, t_cal=256, seed=80)
+    backend = type("B", (FakeBackend,), {})
+    vb.install_kvquant_backend("", device="cuda", scales=sc, backend_cls=backend, impl_cls=FakeImpl)
+    impl = backend.get_impl_cls()(scale=1.0)
+    K, V = make_kv(300, H, D, seed=81, chan_seed=1080)
+    q = torch.zeros((300, 28, D), dtype=torch.float16, device="cuda")
+    impl.forward(types.SimpleNamespace(layer_name="model.layers.1.self_attn.attn"), q, K, V, None,
+                 types.SimpleNamespace(num_actual_tokens=280), q)
+    kq, vq = impl.sent[0]
+    ls = oracle_scales(sc)[1]
+    _, km, krec = quantize_k_rows(np16(K[:280]), ls)
+    vc, vm = quantize_v_rows(np16(V[:280]), np.arange(280), ls)
+    np.testing.assert_array_equal(np16(kq[:280]).view(np.uint16), krec.astype(np.float16).view(np.uint16))
+    pr = np.minimum(np.arange(280), ls.t_cal - 1)
+    L = ls.v_poles.shape[-1]
+    vpol = np.broadcast_to(ls.v_poles[:, pr].transpose(1, 0, 2)[:, :, None, :], (280, H, D, L))
+    vrec = np.take_along_axis(vpol, vc[..., None].astype(np.int64), -1)[..., 0]
+    vrec = np.where(vm, np16(V[:280]), vrec).astype(np.float16)
+    np.testing.assert_array_equal(np16(vq[:280]).view(np.uint16), vrec.view(np.uint16))
+    assert torch.equal(kq[280:], K[280:]) and torch.equal(vq[280:], V[280:])
