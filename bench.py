@@ -287,6 +287,11 @@ def run_ours(args):
     for _ in range(max(1, args.warmup)):
         step()
     torch.cuda.synchronize()
+    # launches of this library's kernels in one step (counted at the C ABI)
+    hxlib.launch_count[0] = 0
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = hxlib.launch_count[0]
     graph = None
     # collectives stay outside graphs this round: N > 1 times eager steps
     use_graph = not args.no_graph and world == 1
@@ -321,7 +326,7 @@ def run_ours(args):
         e1.record()
         torch.cuda.synchronize()
     ms_dev = e0.elapsed_time(e1) / args.steps
-    launches_graph = len(W["per_layer"]) * 3 * args.steps
+    launches_graph = launches_per_step * args.steps
 
     # ---- per-kernel timing (eager steps with events between the launches)
     tstep = make_step(W, world, group, timing)
