@@ -29,7 +29,7 @@ constexpr int NW = 12;           // warps per CTA (one CTA per SM)
 constexpr int NT = NW * 32;
 constexpr int NSTAGE = 3;        // pages in smem per warp (two in flight while one is used)
 constexpr int LISTCAP = 512;     // pages gathered per round
-constexpr int ENTCAP = 128;      // outlier entries staged per page per K|V
+constexpr int ENTCAP = 192;      // outlier entries staged per page per K|V (nuq2 pages hold ~150)
 constexpr int SEGMAX = DS * DD;  // codes bytes per page segment at 4+4 bits
 constexpr int PSZ = 8 * DD + 16; // floats per split partial: O[8][128], m[8], l[8]
 constexpr int MAXSPLIT = 1024;   // splits the final merge stages weights for
@@ -137,6 +137,26 @@ HX_DEVINL void lut16_crumb(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t
 // element offset of (token t, channel d) in a swizzled tile: 16-byte chunks
 // of a row are XOR-permuted by t & 7 so ldmatrix rows hit distinct banks
 HX_DEVINL int tile_off(int t, int d) { return t * DD + ((((d >> 3) ^ (t & 7))) << 3) + (d & 7); }
+
+// Write a page's outlier values over its dequantised tile: the staged entries
+// (at most ENTCAP, two a lane per pass), then any past them from the arena.
+HX_DEVINL void patch_one(uint16_t* tile, uint32_t en, uint32_t* err) {
+  const int et = (en >> 24) & 31, ed = (en >> 16) & 255;
+  if (et < DS && ed < DD) tile[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
+  else set_err(err, HX_DEV_ERR_BOUNDS);
+}
+HX_DEVINL void patch_tile(uint16_t* tile, const uint32_t* staged, const uint32_t* spill, uint32_t cnt, int lane,
+                          uint32_t* err) {
+  const uint32_t ns = min(cnt, (uint32_t)ENTCAP);
+  uint32_t e = lane;
+  for (; e + 32 < ns; e += 64) {
+    const uint32_t a = staged[e], b = staged[e + 32];
+    patch_one(tile, a, err);
+    patch_one(tile, b, err);
+  }
+  if (e < ns) patch_one(tile, staged[e], err);
+  for (e = ENTCAP + lane; e < cnt; e += 32) patch_one(tile, spill[e], err);
+}
 
 template <int BK, int BV>
 __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
@@ -348,12 +368,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
         }
       }
       __syncwarp();
-      for (uint32_t e = lane; e < cntk; e += 32) {
-        uint32_t en = e < ENTCAP ? ws.ent[st][0][e] : p.pool.arena[offk + e];
-        int et = (en >> 24) & 31, ed = (en >> 16) & 255;
-        if (et < DS && ed < DD) ws.tile[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
-        else set_err(p.err, HX_DEV_ERR_BOUNDS);
-      }
+      patch_tile(ws.tile, ws.ent[st][0], p.pool.arena + offk, cntk, lane, p.err);
       __syncwarp();
 
       // ---- S^T = K . Q^T  (16 tokens x 8 head columns), two accumulator chains
@@ -460,12 +475,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
         }
       }
       __syncwarp();
-      for (uint32_t e = lane; e < cntv; e += 32) {
-        uint32_t en = e < ENTCAP ? ws.ent[st][1][e] : p.pool.arena[offv + e];
-        int et = (en >> 24) & 31, ed = (en >> 16) & 255;
-        if (et < DS && ed < DD) ws.tile[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
-        else set_err(p.err, HX_DEV_ERR_BOUNDS);
-      }
+      patch_tile(ws.tile, ws.ent[st][1], p.pool.arena + offv, cntv, lane, p.err);
       __syncwarp();
 
       // ---- O^T += V^T . P^T  (128 channels x 8 head columns)
