@@ -8,11 +8,11 @@
 // src/quest/reference.py:136-168 (softmax(q.K^T * scale) V, fp32 softmax),
 // generalised to grouped-query heads (query head h*G+g reads KV head h).
 //
-// One CTA = (split, KV head, sequence), 12 warps, one CTA per SM; the CTA's
+// One CTA = (split, KV head, sequence), 16 warps, one CTA per SM; the CTA's
 // pages (a balanced share of the selected list) are dealt to the warps. Each
 // warp streams its pages: bulk copies (cp.async.bulk, no multicast) of the
 // page's code segment, its outlier entries and, before t_cal, its per-token V
-// level rows into a 3-stage buffer; LUT dequant of the 16 x 128 K tile into
+// level rows into a 2-stage buffer; LUT dequant of the 16 x 128 K tile into
 // swizzled smem (one prmt-built table address per code), outlier patch,
 // ldmatrix + mma.sync (tokens x heads), online softmax in fp32 (exp2 domain;
 // the running max moves only when a score passes it by 2^8), P split into
@@ -25,11 +25,11 @@ namespace hx {
 
 constexpr int DD = 128;          // head_size
 constexpr int DS = 16;           // page size (tokens)
-constexpr int NW = 12;           // warps per CTA (one CTA per SM)
+constexpr int NW = 16;           // warps per CTA (one CTA per SM, 128 registers a thread)
 constexpr int NT = NW * 32;
-constexpr int NSTAGE = 3;        // pages in smem per warp (two in flight while one is used)
+constexpr int NSTAGE = 2;        // pages in smem per warp (one in flight while one is used)
 constexpr int LISTCAP = 512;     // pages gathered per round
-constexpr int ENTCAP = 192;      // outlier entries staged per page per K|V (nuq2 pages hold ~150)
+constexpr int ENTCAP = 176;      // outlier entries staged per page per K|V (nuq2 pages hold ~150)
 constexpr int SEGMAX = DS * DD;  // codes bytes per page segment at 4+4 bits
 constexpr int PSZ = 8 * DD + 16; // floats per split partial: O[8][128], m[8], l[8]
 constexpr int MAXSPLIT = 1024;   // splits the final merge stages weights for
@@ -180,11 +180,21 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   const int seq_len = p.seq_lens[b];
   const int n = min((seq_len + DS - 1) / DS, p.max_pages);
 
-  // ---- per-CTA tables
-  for (int i = tid; i < NLK * DD; i += NT) {
-    int d = i / NLK, c = i % NLK;
-    sm.klut[NLK * d + 32 * (d >> 6) + c] =
-        c < p.sc.levels_k ? p.sc.k_poles[((int64_t)h * DD + d) * p.sc.levels_k + c] : (uint16_t)0;
+  // ---- per-CTA tables (all of a thread's loads in flight before its stores)
+  {
+    constexpr int PER = (NLK * DD + NT - 1) / NT;
+    uint16_t kv[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT, d = i / NLK, c = i % NLK;
+      kv[u] = (i < NLK * DD && c < p.sc.levels_k) ? p.sc.k_poles[((int64_t)h * DD + d) * p.sc.levels_k + c]
+                                                  : (uint16_t)0;
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT, d = i / NLK, c = i % NLK;
+      if (i < NLK * DD) sm.klut[NLK * d + 32 * (d >> 6) + c] = kv[u];
+    }
   }
   if (tid < NLV)
     sm.vtail[tid] = tid < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + (Tc - 1)) * p.sc.levels_v + tid] : (uint16_t)0;
@@ -599,20 +609,30 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   __syncthreads();
   for (int i = tid; i < G * (DD / 4); i += NT) {
     const int c = i / (DD / 4), d4 = i % (DD / 4);
-    float4 A = make_float4(0.0f, 0.0f, 0.0f, 0.0f), Bv = A;
+    // eight splits' partials in flight per pass, four accumulators
+    float4 acc[4];
+#pragma unroll
+    for (int a4 = 0; a4 < 4; ++a4) acc[a4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     int s = 0;
-    for (; s + 2 <= p.n_splits; s += 2) {
-      const float4 v0 = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)s * PSZ + c * DD) + d4);
-      const float4 v1 = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)(s + 1) * PSZ + c * DD) + d4);
-      const float w0 = wts[s * 8 + c], w1 = wts[(s + 1) * 8 + c];
-      A.x += w0 * v0.x; A.y += w0 * v0.y; A.z += w0 * v0.z; A.w += w0 * v0.w;
-      Bv.x += w1 * v1.x; Bv.y += w1 * v1.y; Bv.z += w1 * v1.z; Bv.w += w1 * v1.w;
+    for (; s + 8 <= p.n_splits; s += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[u] = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)(s + u) * PSZ + c * DD) + d4);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = wts[(s + u) * 8 + c];
+        acc[u & 3].x += w * v[u].x; acc[u & 3].y += w * v[u].y;
+        acc[u & 3].z += w * v[u].z; acc[u & 3].w += w * v[u].w;
+      }
     }
-    if (s < p.n_splits) {
+    for (; s < p.n_splits; ++s) {
       const float4 v0 = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)s * PSZ + c * DD) + d4);
       const float w0 = wts[s * 8 + c];
-      A.x += w0 * v0.x; A.y += w0 * v0.y; A.z += w0 * v0.z; A.w += w0 * v0.w;
+      acc[0].x += w0 * v0.x; acc[0].y += w0 * v0.y; acc[0].z += w0 * v0.z; acc[0].w += w0 * v0.w;
     }
+    const float4 A = make_float4(acc[0].x + acc[2].x, acc[0].y + acc[2].y, acc[0].z + acc[2].z, acc[0].w + acc[2].w);
+    const float4 Bv = make_float4(acc[1].x + acc[3].x, acc[1].y + acc[3].y, acc[1].z + acc[3].z, acc[1].w + acc[3].w);
     const float L = sm.colL[c];
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
     const float4 ov = make_float4((A.x + Bv.x) * inv, (A.y + Bv.y) * inv, (A.z + Bv.z) * inv, (A.w + Bv.w) * inv);
