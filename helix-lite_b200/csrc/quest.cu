@@ -277,14 +277,25 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     int bh, j0, cnt, sinks;
     int64_t phys;
   };
-  auto plan = [&](int64_t it) -> Bat {
+  // The planner walks the warp's batches in order, so (b, h) and the batch
+  // index advance by counting, and a sequence's length is read once per (b, h):
+  // no division and no dependent global load per batch.
+  int pl_bh = -1, pl_jb = 0, pl_n = 0;
+  auto plan_next = [&](bool first, int64_t it) -> Bat {
+    if (first) {
+      pl_bh = (int)(it / nb);
+      pl_jb = (int)(it % nb);
+    } else if (++pl_jb == nb) {
+      pl_jb = 0;
+      ++pl_bh;
+    }
     Bat r;
-    r.bh = (int)(it / nb);
-    r.j0 = (int)(it % nb) * kQPB;
+    r.bh = pl_bh;
+    r.j0 = pl_jb * kQPB;
     const int b = r.bh / H;
-    const int n = min((seq_lens[b] + S - 1) / S, max_pages);
-    r.cnt = max(0, min(kQPB, n - r.j0));
-    r.sinks = min(max(sinks_req, 0), n);
+    if (first || pl_jb == 0) pl_n = min((seq_lens[b] + S - 1) / S, max_pages);
+    r.cnt = max(0, min(kQPB, pl_n - r.j0));
+    r.sinks = min(max(sinks_req, 0), pl_n);
     const int j = r.j0 + lane;
     r.phys = (lane < r.cnt) ? (bt ? (int64_t)bt[(int64_t)b * bt_stride + j] : (int64_t)j) : 0;
     return r;
@@ -315,9 +326,9 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   const int64_t g0 = gw * per;
   const int nk = (int)max((int64_t)0, min(per, total - g0));
   Bat p0 = {0, 0, 0, 0, 0}, p1 = {0, 0, 0, 0, 0}, p2 = {0, 0, 0, 0, 0};
-  if (nk > 0) p0 = plan(g0);
-  if (nk > 1) p1 = plan(g0 + 1);
-  if (nk > 2) p2 = plan(g0 + 2);
+  if (nk > 0) p0 = plan_next(true, g0);
+  if (nk > 1) p1 = plan_next(false, 0);
+  if (nk > 2) p2 = plan_next(false, 0);
   issue(p0, 0);
   issue(p1, 1 % kQStages);
   int cur_bh = -1;
@@ -330,7 +341,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     // reads overlap this batch's work)
     if (k + 2 < nk) issue(p2, (k + 2) % kQStages);
     Bat p3 = {0, 0, 0, 0, 0};
-    if (k + 3 < nk) p3 = plan(g0 + k + 3);
+    if (k + 3 < nk) p3 = plan_next(false, 0);
     const Bat cb = p0;
     if (cb.cnt > 0) {
       const int b = cb.bh / H, h = cb.bh % H;
