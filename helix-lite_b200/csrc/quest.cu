@@ -250,8 +250,40 @@ constexpr int kQStages = 3;  // batches in smem per warp (2 in flight while one 
 struct __align__(128) QuestSmem {
   uint16_t rec[kQW][kQStages][kQPB][256];  // [warp][stage][page][min 128 | max 128]
   uint64_t bar[kQW][kQStages];
-  float qp[kQW][128], qn[kQW][128];
 };
+
+// group_terms for channels 4 lane .. 4 lane + 3 (D = 128): one 8-byte load
+// per query head, the same per-channel arithmetic.
+HX_DEVINL void group_terms4(const uint16_t* __restrict__ q, int64_t qbase, int G, int mode, int lane, float* qp,
+                            float* qn) {
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f}, t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+  for (int g = 0; g < G; ++g) {
+    const uint2 w = *reinterpret_cast<const uint2*>(q + qbase + (int64_t)g * 128 + 4 * lane);
+    const float x[4] = {h2f((uint16_t)(w.x & 0xffff)), h2f((uint16_t)(w.x >> 16)), h2f((uint16_t)(w.y & 0xffff)),
+                        h2f((uint16_t)(w.y >> 16))};
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      if (mode == 0) {
+        s[v] = __fadd_rn(s[v], x[v] > 0.0f ? x[v] : 0.0f);
+        t[v] = __fadd_rn(t[v], x[v] < 0.0f ? x[v] : 0.0f);
+      } else {
+        s[v] = __fadd_rn(s[v], x[v]);
+      }
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    if (mode == 0) {
+      qp[v] = s[v];
+      qn[v] = t[v];
+    } else {
+      const float m = h2f(f2h(__fdiv_rn(s[v], (float)G)));
+      qp[v] = m > 0.0f ? m : 0.0f;
+      qn[v] = m < 0.0f ? m : 0.0f;
+    }
+  }
+}
 
 __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     const uint16_t* __restrict__ q, int B, int H, int G, int mode, const uint16_t* __restrict__ kmin,
@@ -344,20 +376,9 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     if (k + 3 < nk) p3 = plan_next(false, 0);
     const Bat cb = p0;
     if (cb.cnt > 0) {
-      const int b = cb.bh / H, h = cb.bh % H;
       if (cb.bh != cur_bh) {
-        for (int d = lane; d < 128; d += 32) {
-          float a, c;
-          group_terms(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, 128, mode, d, a, c);
-          sm.qp[warp][d] = a;
-          sm.qn[warp][d] = c;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          qp[v] = sm.qp[warp][4 * lane + v];
-          qn[v] = sm.qn[warp][4 * lane + v];
-        }
+        const int b = cb.bh / H, h = cb.bh % H;
+        group_terms4(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, mode, lane, qp, qn);
         cur_bh = cb.bh;
       }
       if (!dead && !mbar_wait(&sm.bar[warp][st], (phase >> st) & 1u)) {
@@ -396,10 +417,19 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
       part[0] = __fadd_rn(part[0], __shfl_xor_sync(0xffffffffu, part[0], 2));
       part[0] = __fadd_rn(part[0], __shfl_xor_sync(0xffffffffu, part[0], 1));
       const int u = lane >> 2, j = cb.j0 + u;
-      if ((lane & 3) == 0 && u < cb.cnt) {
-        scores[(int64_t)cb.bh * max_pages + j] = part[0];
-        if (hist && j >= cb.sinks)
-          atomicAdd(&hist[(int64_t)cb.bh * 2 * kBins + (order_key(part[0]) >> 20)], 1u);
+      const bool own = (lane & 3) == 0 && u < cb.cnt;
+      if (own) scores[(int64_t)cb.bh * max_pages + j] = part[0];
+      if (hist) {
+        // a (b, h)'s scores crowd into a few bins: pages of the batch that
+        // share a bin go as one atomic, or the same-address atomics serialise
+        const bool counted = own && j >= cb.sinks;
+        const uint32_t bin = order_key(part[0]) >> 20;
+        const uint32_t act = __ballot_sync(0xffffffffu, counted);
+        if (counted) {
+          const uint32_t peers = __match_any_sync(act, bin);
+          if (lane == __ffs(peers) - 1)
+            atomicAdd(&hist[(int64_t)cb.bh * 2 * kBins + bin], (uint32_t)__popc(peers));
+        }
       }
     }
     __syncwarp();
