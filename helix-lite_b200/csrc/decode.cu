@@ -70,8 +70,9 @@ struct __align__(256) WarpSmem {
 
 struct __align__(256) CtaSmem {
   WarpSmem w[NW];
-  alignas(256) uint16_t klut[16 * DD + 64];  // per-channel K levels (bank-spread, 256-aligned)
+  alignas(256) uint16_t klut[16 * DD + 64];  // K tables (bank-spread, 256-aligned; layout at the fill)
   alignas(256) uint16_t vtail[16];           // V levels at positions >= t_cal (256-aligned)
+  alignas(256) uint32_t vpair[16];           // nuq2: the same as level pairs (entry c0 | c1 << 2)
   int32_t pages[LISTCAP];
   int32_t phys[LISTCAP];
   uint4 dir[LISTCAP][2];                // K and V directory records of each page
@@ -114,6 +115,30 @@ HX_DEVINL uint4 lut8_nib(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t o
                     pack_u16x2(v[6], v[7]));
 }
 
+HX_DEVINL uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// 16 levels for 16 consecutive 2-bit codes of word w from level-pair tables:
+// a nibble (two codes) picks one 4-byte entry holding both levels, so each
+// load yields two channels. tab(pair n) = base + off + TSTRIDE * n, entry
+// 4 * nibble; as in lut8_nib only base's low byte is replaced.
+template <int TSTRIDE>
+HX_DEVINL void lut8_pair(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t off, uint4& o0, uint4& o1) {
+  const uint32_t lo = ((w << 2) & 0x3C3C3C3Cu) | lowbits;  // 4 * low nibble: codes 4k, 4k+1
+  const uint32_t hi = ((w >> 2) & 0x3C3C3C3Cu) | lowbits;  // 4 * high nibble: codes 4k+2, 4k+3
+  uint32_t v[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[2 * k] = lds32(prmt(lo, base, 0x7650u | k) + off + TSTRIDE * (2 * k));
+    v[2 * k + 1] = lds32(prmt(hi, base, 0x7650u | k) + off + TSTRIDE * (2 * k + 1));
+  }
+  o0 = make_uint4(v[0], v[1], v[2], v[3]);
+  o1 = make_uint4(v[4], v[5], v[6], v[7]);
+}
+
 // 16 levels for 16 consecutive 2-bit codes of word w, as two 8-wide chunks.
 template <int TSTRIDE>
 HX_DEVINL void lut16_crumb(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t off, uint4& o0,
@@ -134,9 +159,13 @@ HX_DEVINL void lut16_crumb(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t
                   pack_u16x2(v[14], v[15]));
 }
 
-// element offset of (token t, channel d) in a swizzled tile: 16-byte chunks
-// of a row are XOR-permuted by t & 7 so ldmatrix rows hit distinct banks
-HX_DEVINL int tile_off(int t, int d) { return t * DD + ((((d >> 3) ^ (t & 7))) << 3) + (d & 7); }
+// Element offset of 16-byte chunk c (channels 8c .. 8c+7) of token t in a
+// swizzled tile: position c ^ (t & 7) ^ 4 (c >> 3). Eight consecutive rows at
+// one chunk (an ldmatrix phase) land in 8 distinct bank groups, and so do the
+// dequant stores, where a wavefront's 8 lanes are tokens 4j .. 4j+3 x both
+// row halves.
+HX_DEVINL int tile_chunk(int t, int c) { return t * DD + ((c ^ (t & 7) ^ ((c >> 3) << 2)) << 3); }
+HX_DEVINL int tile_off(int t, int d) { return tile_chunk(t, d >> 3) + (d & 7); }
 
 // Write a page's outlier values over its dequantised tile: the staged entries
 // (at most ENTCAP, two a lane per pass), then any past them from the arena.
@@ -180,30 +209,55 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   const int seq_len = p.seq_lens[b];
   const int n = min((seq_len + DS - 1) / DS, p.max_pages);
 
-  // ---- per-CTA tables (all of a thread's loads in flight before its stores)
-  {
-    constexpr int PER = (NLK * DD + NT - 1) / NT;
+  // ---- per-CTA tables (all of a thread's loads in flight before its stores).
+  // nuq4 K: channel d's 16 levels (32 B) at byte 32 d + 32 (d >> 5). nuq2 K:
+  // channel pair P = (2P, 2P+1) as 16 level pairs (64 B; entry e holds the
+  // levels of codes e & 3 and e >> 2) at byte 64 P + 64 (P >> 5). Either way the
+  // tables a dequant load touches at once sit in disjoint bank windows.
+  auto kpole = [&](int d, int c) -> uint16_t {
+    return c < p.sc.levels_k ? p.sc.k_poles[((int64_t)h * DD + d) * p.sc.levels_k + c] : (uint16_t)0;
+  };
+  auto vtail_level = [&](int c) -> uint16_t {
+    return c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + (Tc - 1)) * p.sc.levels_v + c] : (uint16_t)0;
+  };
+  if (BK == 4) {
+    constexpr int PER = (16 * DD + NT - 1) / NT;
     uint16_t kv[PER];
 #pragma unroll
     for (int u = 0; u < PER; ++u) {
-      const int i = tid + u * NT, d = i / NLK, c = i % NLK;
-      kv[u] = (i < NLK * DD && c < p.sc.levels_k) ? p.sc.k_poles[((int64_t)h * DD + d) * p.sc.levels_k + c]
-                                                  : (uint16_t)0;
+      const int i = tid + u * NT;
+      kv[u] = i < 16 * DD ? kpole(i >> 4, i & 15) : (uint16_t)0;
     }
 #pragma unroll
     for (int u = 0; u < PER; ++u) {
-      const int i = tid + u * NT, d = i / NLK, c = i % NLK;
-      if (i < NLK * DD) sm.klut[NLK * d + 32 * (d >> 6) + c] = kv[u];
+      const int i = tid + u * NT, d = i >> 4;
+      if (i < 16 * DD) sm.klut[16 * d + 16 * (d >> 5) + (i & 15)] = kv[u];
+    }
+  } else {
+    constexpr int PER = (16 * (DD / 2) + NT - 1) / NT;
+    uint32_t kv[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT, P = i >> 4, e = i & 15;
+      kv[u] = i < 16 * (DD / 2) ? pack_u16x2(kpole(2 * P, e & 3), kpole(2 * P + 1, e >> 2)) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT, P = i >> 4;
+      if (i < 16 * (DD / 2)) reinterpret_cast<uint32_t*>(sm.klut)[16 * P + 16 * (P >> 5) + (i & 15)] = kv[u];
     }
   }
-  if (tid < NLV)
-    sm.vtail[tid] = tid < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + (Tc - 1)) * p.sc.levels_v + tid] : (uint16_t)0;
+  if (tid < NLV) sm.vtail[tid] = vtail_level(tid);
+  if (BV == 2 && tid >= 32 && tid < 48) sm.vpair[tid - 32] = pack_u16x2(vtail_level((tid - 32) & 3), vtail_level((tid - 32) >> 2));
   WarpSmem& ws = sm.w[warp];
   if (lane == 0) {
     for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
     fence_mbar_init();
   }
 
+  // dequant lanes: token t = lane >> 1, row half = lane & 1; x0 = which
+  // 16-byte chunk of its half row (nuq4) the lane reads first is cx0
+  const int t = lane >> 1, half = lane & 1, cx0 = (lane >> 2) & 1;
   // query fragments (B operand, k = channel, n = head column)
   const int g = lane >> 2, qd = lane & 3;
   uint32_t bq[8][2];
@@ -348,32 +402,39 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       const int pos0 = (p.page_begin + j) * DS;
       const int valid = seq_len - j * DS;  // tokens of this page inside the sequence
 
-      const int t = lane & 15, half = lane >> 4;
-      // ---- K tile: per-channel LUT (lane = token t, half of the channels)
+      // ---- K tile: per-channel tables (lane = token t, half of the channels)
       {
         const uint8_t* rowp = ws.raw[st] + t * RBK + half * (RBK / 2);
-        // half 1's tables start 64 tables + 64 bytes later: its low address byte is 0x40
-        const uint32_t kbase = smem_u32(sm.klut) + (half ? (uint32_t)(64 * 2 * NLK + 64) : 0u);
-        const uint32_t low = half ? 0x40404040u : 0u;
         if (BK == 4) {
-          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
-          const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
-          const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          // the half row's two 16-byte chunks in the lane's order cx0, cx0 ^ 1, so
+          // the 8 lanes of a wavefront read 8 distinct bank groups
+          const uint4 ca = *reinterpret_cast<const uint4*>(rowp + 16 * cx0);
+          const uint4 cb = *reinterpret_cast<const uint4*>(rowp + 16 * (cx0 ^ 1));
+          const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
-          for (int w8 = 0; w8 < 8; ++w8) {
-            const uint4 o4 = lut8_nib<32>(wv[w8], low, kbase, 32u * 8u * (uint32_t)w8);
-            const int chunk = (8 * half + w8) ^ (t & 7);
-            *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
+          for (int j = 0; j < 2; ++j) {
+            // channels 64 half + 32 x .. +31: tables at klut + 2048 half + 1024 x
+            // + 64 half + 32 x (+ 256 per 8 channels); the last term is the low byte
+            const int x = cx0 ^ j;
+            const uint32_t base = smem_u32(sm.klut) + 2048u * half + 1024u * x;
+            const uint32_t low = (64u * half + 32u * x) * 0x01010101u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 o4 = lut8_nib<32>(wv[4 * j + i], low, base, 256u * i);
+              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 4 * x + i)) = o4;
+            }
           }
         } else {
+          // pair P = 32 half + 8 w + n at klut + 2048 half + 64 half + 512 w + 64 n
           const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
           const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+          const uint32_t base = smem_u32(sm.klut) + 2048u * half, low = 64u * half * 0x01010101u;
 #pragma unroll
           for (int w4 = 0; w4 < 4; ++w4) {
             uint4 o0, o1;
-            lut16_crumb<8>(wv[w4], low, kbase, 8u * 16u * (uint32_t)w4, o0, o1);
-            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4) ^ (t & 7)) * 8)) = o0;
-            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4 + 1) ^ (t & 7)) * 8)) = o1;
+            lut8_pair<64>(wv[w4], low, base, 512u * (uint32_t)w4, o0, o1);
+            *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4)) = o0;
+            *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4 + 1)) = o1;
           }
         }
       }
@@ -387,8 +448,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       for (int ks = 0; ks < 8; ++ks) {
         uint32_t a[4];
         const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int chunk = (2 * ks + (lane >> 4)) ^ (r & 7);
-        ldmatrix_x4(a, ws.tile + r * DD + chunk * 8);
+        ldmatrix_x4(a, ws.tile + tile_chunk(r, 2 * ks + (lane >> 4)));
         if (ks & 1) mma_16816(sb, a, bq[ks][0], bq[ks][1]);
         else mma_16816(sa, a, bq[ks][0], bq[ks][1]);
       }
@@ -436,8 +496,9 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       const uint32_t bl0 = movmatrix_trans(plo_top), bl1 = movmatrix_trans(plo_bot);
 
       // ---- V tile: per-token LUT (row min(pos, t_cal - 1))
+      const bool vshared = pos0 >= Tc;
       uint32_t vbase, vlow;
-      if (pos0 >= Tc) {
+      if (vshared) {
         vbase = smem_u32(sm.vtail);  // one table for every token
         vlow = 0u;
       } else {
@@ -463,24 +524,38 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       {
         const uint8_t* rowp = ws.raw[st] + DS * RBK + t * RBV + half * (RBV / 2);
         if (BV == 4) {
-          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
-          const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + 16);
-          const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const uint4 ca = *reinterpret_cast<const uint4*>(rowp + 16 * cx0);
+          const uint4 cb = *reinterpret_cast<const uint4*>(rowp + 16 * (cx0 ^ 1));
+          const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
-          for (int w8 = 0; w8 < 8; ++w8) {
-            const uint4 o4 = lut8_nib<0>(wv[w8], vlow, vbase, 0u);
-            const int chunk = (8 * half + w8) ^ (t & 7);
-            *reinterpret_cast<uint4*>(ws.tile + t * DD + chunk * 8) = o4;
+          for (int j = 0; j < 2; ++j) {
+            const int x = cx0 ^ j;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 o4 = lut8_nib<0>(wv[4 * j + i], vlow, vbase, 0u);
+              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 4 * x + i)) = o4;
+            }
           }
         } else {
           const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
           const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+          if (vshared) {  // one level-pair table for every token
+            const uint32_t pb = smem_u32(sm.vpair);
 #pragma unroll
-          for (int w4 = 0; w4 < 4; ++w4) {
-            uint4 o0, o1;
-            lut16_crumb<0>(wv[w4], vlow, vbase, 0u, o0, o1);
-            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4) ^ (t & 7)) * 8)) = o0;
-            *reinterpret_cast<uint4*>(ws.tile + t * DD + (((8 * half + 2 * w4 + 1) ^ (t & 7)) * 8)) = o1;
+            for (int w4 = 0; w4 < 4; ++w4) {
+              uint4 o0, o1;
+              lut8_pair<0>(wv[w4], 0u, pb, 0u, o0, o1);
+              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4)) = o0;
+              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4 + 1)) = o1;
+            }
+          } else {
+#pragma unroll
+            for (int w4 = 0; w4 < 4; ++w4) {
+              uint4 o0, o1;
+              lut16_crumb<0>(wv[w4], vlow, vbase, 0u, o0, o1);
+              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4)) = o0;
+              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4 + 1)) = o1;
+            }
           }
         }
       }
@@ -493,8 +568,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       for (int mt = 0; mt < 8; ++mt) {
         uint32_t a[4];
         const int r = (lane & 7) + ((lane >> 4) & 1) * 8;
-        const int chunk = (2 * mt + ((lane >> 3) & 1)) ^ (r & 7);
-        ldmatrix_x4_trans(a, ws.tile + r * DD + chunk * 8);
+        ldmatrix_x4_trans(a, ws.tile + tile_chunk(r, 2 * mt + ((lane >> 3) & 1)));
         mma_16816(oacc[mt], a, bh0, bh1);
         mma_16816(oacc[mt], a, bl0, bl1);
       }
