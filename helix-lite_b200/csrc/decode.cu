@@ -115,6 +115,19 @@ HX_DEVINL uint4 lut8_nib(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t o
                     pack_u16x2(v[6], v[7]));
 }
 
+HX_DEVINL void sts128(uint32_t addr, const uint4& v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+}
+HX_DEVINL void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+HX_DEVINL void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
 HX_DEVINL uint32_t lds32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
@@ -159,32 +172,38 @@ HX_DEVINL void lut16_crumb(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t
                   pack_u16x2(v[14], v[15]));
 }
 
-// Element offset of 16-byte chunk c (channels 8c .. 8c+7) of token t in a
-// swizzled tile: position c ^ (t & 7) ^ 4 (c >> 3). Eight consecutive rows at
-// one chunk (an ldmatrix phase) land in 8 distinct bank groups, and so do the
-// dequant stores, where a wavefront's 8 lanes are tokens 4j .. 4j+3 x both
-// row halves.
-HX_DEVINL int tile_chunk(int t, int c) { return t * DD + ((c ^ (t & 7) ^ ((c >> 3) << 2)) << 3); }
-HX_DEVINL int tile_off(int t, int d) { return tile_chunk(t, d >> 3) + (d & 7); }
+// Tile layout: 16 tokens x 128 channels fp16, 256 bytes a token; 16-byte chunk
+// c (channels 8c .. 8c+7) of token t sits at position c ^ (t & 7) ^ 4 (c >> 3)
+// of its row. Eight consecutive rows at one chunk (an ldmatrix phase) land in
+// 8 distinct bank groups, and so do the dequant stores, where a wavefront's 8
+// lanes are tokens 4j .. 4j+3 x both row halves.
 
 // Write a page's outlier values over its dequantised tile: the staged entries
 // (at most ENTCAP, two a lane per pass), then any past them from the arena.
-HX_DEVINL void patch_one(uint16_t* tile, uint32_t en, uint32_t* err) {
-  const int et = (en >> 24) & 31, ed = (en >> 16) & 255;
-  if (et < DS && ed < DD) tile[tile_off(et, ed)] = (uint16_t)(en & 0xffffu);
-  else set_err(err, HX_DEV_ERR_BOUNDS);
+// An entry is fp16 | channel << 16 | token << 24, so x = en >> 16 holds
+// token << 8 | channel and the tile byte offset 256 t + 16 (c ^ (t & 7) ^
+// 4 (c >> 3)) + 2 (d & 7) is (x & 0xF00 | 2 x & 0xFE) ^ (x >> 4 & 0x70) ^
+// (x & 0x40). The masks keep every offset inside the 4 KB tile; an entry with
+// token >= 16 or channel >= 128 (bits 0xF080 of x) is flagged once per tile.
+HX_DEVINL void patch_one(uint32_t tile0, uint32_t en, uint32_t& bad) {
+  const uint32_t x = en >> 16;
+  const uint32_t off = (((x & 0xF00u) | ((x << 1) & 0xFEu)) ^ ((x >> 4) & 0x70u)) ^ (x & 0x40u);
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(tile0 + off), "h"((uint16_t)(en & 0xffffu)));
+  bad |= x & 0xF080u;
 }
-HX_DEVINL void patch_tile(uint16_t* tile, const uint32_t* staged, const uint32_t* spill, uint32_t cnt, int lane,
+HX_DEVINL void patch_tile(uint32_t tile0, const uint32_t* staged, const uint32_t* spill, uint32_t cnt, int lane,
                           uint32_t* err) {
   const uint32_t ns = min(cnt, (uint32_t)ENTCAP);
+  uint32_t bad = 0;
   uint32_t e = lane;
   for (; e + 32 < ns; e += 64) {
     const uint32_t a = staged[e], b = staged[e + 32];
-    patch_one(tile, a, err);
-    patch_one(tile, b, err);
+    patch_one(tile0, a, bad);
+    patch_one(tile0, b, bad);
   }
-  if (e < ns) patch_one(tile, staged[e], err);
-  for (e = ENTCAP + lane; e < cnt; e += 32) patch_one(tile, spill[e], err);
+  if (e < ns) patch_one(tile0, staged[e], bad);
+  for (e = ENTCAP + lane; e < cnt; e += 32) patch_one(tile0, spill[e], bad);
+  if (bad) set_err(err, HX_DEV_ERR_BOUNDS);
 }
 
 template <int BK, int BV>
@@ -258,6 +277,19 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   // dequant lanes: token t = lane >> 1, row half = lane & 1; x0 = which
   // 16-byte chunk of its half row (nuq4) the lane reads first is cx0
   const int t = lane >> 1, half = lane & 1, cx0 = (lane >> 2) & 1;
+  // Tile byte addresses (the tile is 256-aligned): chunk c of token t is at
+  // tile + 256 t + 16 (c ^ (t & 7) ^ 4 (c >> 3)). With c = 8 half + low, a
+  // lane's dequant store is tw ^ 16 low, and each ldmatrix phase reads a lane
+  // base ^ 16 k(step) with k(s) = 2 s ^ 4 (s >> 2).
+  const uint32_t tile0 = smem_u32(ws.tile);
+  const uint32_t tw = tile0 + 256u * t + 16u * ((8 * half) ^ (4 * half) ^ (t & 7));
+  const uint32_t tw4 = tw ^ (64u * cx0);  // nuq4: chunk order cx0, cx0 ^ 1
+  uint32_t tqk, tpv;
+  {
+    const int rk = (lane & 7) + ((lane >> 3) & 1) * 8, rv = (lane & 7) + ((lane >> 4) & 1) * 8;
+    tqk = tile0 + 256u * rk + 16u * ((lane >> 4) ^ (rk & 7));
+    tpv = tile0 + 256u * rv + 16u * (((lane >> 3) & 1) ^ (rv & 7));
+  }
   // query fragments (B operand, k = channel, n = head column)
   const int g = lane >> 2, qd = lane & 3;
   uint32_t bq[8][2];
@@ -419,10 +451,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
             const uint32_t base = smem_u32(sm.klut) + 2048u * half + 1024u * x;
             const uint32_t low = (64u * half + 32u * x) * 0x01010101u;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 o4 = lut8_nib<32>(wv[4 * j + i], low, base, 256u * i);
-              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 4 * x + i)) = o4;
-            }
+            for (int i = 0; i < 4; ++i) sts128(tw4 ^ (64u * j + 16u * i), lut8_nib<32>(wv[4 * j + i], low, base, 256u * i));
           }
         } else {
           // pair P = 32 half + 8 w + n at klut + 2048 half + 64 half + 512 w + 64 n
@@ -433,13 +462,13 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
           for (int w4 = 0; w4 < 4; ++w4) {
             uint4 o0, o1;
             lut8_pair<64>(wv[w4], low, base, 512u * (uint32_t)w4, o0, o1);
-            *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4)) = o0;
-            *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4 + 1)) = o1;
+            sts128(tw ^ (32u * w4), o0);
+            sts128(tw ^ (32u * w4 + 16u), o1);
           }
         }
       }
       __syncwarp();
-      patch_tile(ws.tile, ws.ent[st][0], p.pool.arena + offk, cntk, lane, p.err);
+      patch_tile(tile0, ws.ent[st][0], p.pool.arena + offk, cntk, lane, p.err);
       __syncwarp();
 
       // ---- S^T = K . Q^T  (16 tokens x 8 head columns), two accumulator chains
@@ -447,8 +476,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         uint32_t a[4];
-        const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
-        ldmatrix_x4(a, ws.tile + tile_chunk(r, 2 * ks + (lane >> 4)));
+        ldsm_x4(a, tqk ^ (16u * ((2 * ks) ^ (4 * (ks >> 2)))));
         if (ks & 1) mma_16816(sb, a, bq[ks][0], bq[ks][1]);
         else mma_16816(sa, a, bq[ks][0], bq[ks][1]);
       }
@@ -528,14 +556,9 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
           const uint4 cb = *reinterpret_cast<const uint4*>(rowp + 16 * (cx0 ^ 1));
           const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int x = cx0 ^ j;
+          for (int j = 0; j < 2; ++j)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 o4 = lut8_nib<0>(wv[4 * j + i], vlow, vbase, 0u);
-              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 4 * x + i)) = o4;
-            }
-          }
+            for (int i = 0; i < 4; ++i) sts128(tw4 ^ (64u * j + 16u * i), lut8_nib<0>(wv[4 * j + i], vlow, vbase, 0u));
         } else {
           const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
           const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
@@ -545,30 +568,29 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
             for (int w4 = 0; w4 < 4; ++w4) {
               uint4 o0, o1;
               lut8_pair<0>(wv[w4], 0u, pb, 0u, o0, o1);
-              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4)) = o0;
-              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4 + 1)) = o1;
+              sts128(tw ^ (32u * w4), o0);
+              sts128(tw ^ (32u * w4 + 16u), o1);
             }
           } else {
 #pragma unroll
             for (int w4 = 0; w4 < 4; ++w4) {
               uint4 o0, o1;
               lut16_crumb<0>(wv[w4], vlow, vbase, 0u, o0, o1);
-              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4)) = o0;
-              *reinterpret_cast<uint4*>(ws.tile + tile_chunk(t, 8 * half + 2 * w4 + 1)) = o1;
+              sts128(tw ^ (32u * w4), o0);
+              sts128(tw ^ (32u * w4 + 16u), o1);
             }
           }
         }
       }
       __syncwarp();
-      patch_tile(ws.tile, ws.ent[st][1], p.pool.arena + offv, cntv, lane, p.err);
+      patch_tile(tile0, ws.ent[st][1], p.pool.arena + offv, cntv, lane, p.err);
       __syncwarp();
 
       // ---- O^T += V^T . P^T  (128 channels x 8 head columns)
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
         uint32_t a[4];
-        const int r = (lane & 7) + ((lane >> 4) & 1) * 8;
-        ldmatrix_x4_trans(a, ws.tile + tile_chunk(r, 2 * mt + ((lane >> 3) & 1)));
+        ldsm_x4_trans(a, tpv ^ (16u * ((2 * mt) ^ (4 * (mt >> 2)))));
         mma_16816(oacc[mt], a, bh0, bh1);
         mma_16816(oacc[mt], a, bl0, bl1);
       }
