@@ -29,7 +29,7 @@ constexpr int NW = 16;           // warps per CTA (one CTA per SM, 128 registers
 constexpr int NT = NW * 32;
 constexpr int NSTAGE = 2;        // pages in smem per warp (one in flight while one is used)
 constexpr int LISTCAP = 512;     // pages gathered per round
-constexpr int ENTCAP = 176;      // outlier entries staged per page per K|V (nuq2 pages hold ~150)
+constexpr int ENTCAP = 352;      // outlier entries staged per page, K's then V's (nuq2 pages: ~100 + ~150)
 constexpr int SEGMAX = DS * DD;  // codes bytes per page segment at 4+4 bits
 constexpr int PSZ = 8 * DD + 16; // floats per split partial: O[8][128], m[8], l[8]
 constexpr int MAXSPLIT = 1024;   // splits the final merge stages weights for
@@ -61,7 +61,7 @@ struct DecodeParams {
 
 struct __align__(256) WarpSmem {
   uint8_t raw[NSTAGE][SEGMAX];          // code segments
-  uint32_t ent[NSTAGE][2][ENTCAP];      // [stage][K|V] outlier entries
+  uint32_t ent[NSTAGE][ENTCAP];         // [stage] K entries, then V entries from a 16-byte boundary
   uint16_t tile[DS * DD];               // dequantised K, then V (swizzled rows)
   alignas(256) uint16_t vlut[DS * 16];  // per-token V levels of the current page (256-aligned)
   alignas(256) uint16_t vp[NSTAGE][DS * 16];  // per-token V levels copied with each page's codes
@@ -178,8 +178,8 @@ HX_DEVINL void lut16_crumb(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t
 // 8 distinct bank groups, and so do the dequant stores, where a wavefront's 8
 // lanes are tokens 4j .. 4j+3 x both row halves.
 
-// Write a page's outlier values over its dequantised tile: the staged entries
-// (at most ENTCAP, two a lane per pass), then any past them from the arena.
+// Write a page's outlier values over its dequantised tile: the first nst
+// entries from the staging buffer, any past them from the arena.
 // An entry is fp16 | channel << 16 | token << 24, so x = en >> 16 holds
 // token << 8 | channel and the tile byte offset 256 t + 16 (c ^ (t & 7) ^
 // 4 (c >> 3)) + 2 (d & 7) is (x & 0xF00 | 2 x & 0xFE) ^ (x >> 4 & 0x70) ^
@@ -191,20 +191,23 @@ HX_DEVINL void patch_one(uint32_t tile0, uint32_t en, uint32_t& bad) {
   asm volatile("st.shared.u16 [%0], %1;" ::"r"(tile0 + off), "h"((uint16_t)(en & 0xffffu)));
   bad |= x & 0xF080u;
 }
-HX_DEVINL void patch_tile(uint32_t tile0, const uint32_t* staged, const uint32_t* spill, uint32_t cnt, int lane,
-                          uint32_t* err) {
-  const uint32_t ns = min(cnt, (uint32_t)ENTCAP);
+HX_DEVINL void patch_tile(uint32_t tile0, const uint32_t* staged, const uint32_t* spill, uint32_t cnt, uint32_t nst,
+                          int lane, uint32_t* err) {
+  const uint32_t ns = min(cnt, nst);
   uint32_t bad = 0;
-  uint32_t e = lane;
-  for (; e + 32 < ns; e += 64) {
-    const uint32_t a = staged[e], b = staged[e + 32];
-    patch_one(tile0, a, bad);
-    patch_one(tile0, b, bad);
+#pragma unroll 1
+  for (uint32_t e = lane; e < ns; e += 32) patch_one(tile0, staged[e], bad);
+  if (cnt > nst) {  // warp-uniform; entries past the staged ones
+#pragma unroll 1
+    for (uint32_t e = nst + lane; e < cnt; e += 32) patch_one(tile0, spill[e], bad);
   }
-  if (e < ns) patch_one(tile0, staged[e], bad);
-  for (e = ENTCAP + lane; e < cnt; e += 32) patch_one(tile0, spill[e], bad);
   if (bad) set_err(err, HX_DEV_ERR_BOUNDS);
 }
+
+// Entries staged for a page: K's (rounded up to whole 16-byte copies), then
+// V's in what room is left; the arena serves the rest.
+HX_DEVINL uint32_t stage_k(uint32_t cntk) { return min((cntk + 3u) & ~3u, (uint32_t)ENTCAP); }
+HX_DEVINL uint32_t stage_v(uint32_t ek, uint32_t cntv) { return min((cntv + 3u) & ~3u, (uint32_t)ENTCAP - ek); }
 
 template <int BK, int BV>
 __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
@@ -399,16 +402,15 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
         const int li = warp + NW * k;
         const int pp = sm.phys[li];
         const uint4 dk = sm.dir[li][0], dv = sm.dir[li][1];
-        const uint32_t ek = min((dk.z + 3u) & ~3u, (uint32_t)ENTCAP);
-        const uint32_t ev = min((dv.z + 3u) & ~3u, (uint32_t)ENTCAP);
+        const uint32_t ek = stage_k(dk.z), ev = stage_v(ek, dv.z);
         const int pos0 = (p.page_begin + sm.pages[li]) * DS;
         const bool vb = v_bulk(pos0);
         constexpr uint32_t VPB = 2u * DS * NLV;
         fence_proxy_async();
         mbar_arrive_expect_tx(&ws.bar[st], SEG + 4u * (ek + ev) + (vb ? VPB : 0u));
         bulk_g2s(ws.raw[st], p.pool.codes + ((int64_t)h * NB + pp) * SEG, SEG, &ws.bar[st]);
-        if (ek) bulk_g2s(ws.ent[st][0], p.pool.arena + dk.x, 4u * ek, &ws.bar[st]);
-        if (ev) bulk_g2s(ws.ent[st][1], p.pool.arena + dv.x, 4u * ev, &ws.bar[st]);
+        if (ek) bulk_g2s(ws.ent[st], p.pool.arena + dk.x, 4u * ek, &ws.bar[st]);
+        if (ev) bulk_g2s(ws.ent[st] + ek, p.pool.arena + dv.x, 4u * ev, &ws.bar[st]);
         if (vb) bulk_g2s(ws.vp[st], v_rows(pos0), VPB, &ws.bar[st]);
       }
     };
@@ -468,7 +470,8 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
         }
       }
       __syncwarp();
-      patch_tile(tile0, ws.ent[st][0], p.pool.arena + offk, cntk, lane, p.err);
+      const uint32_t ek = stage_k(cntk);  // K entries staged; V's follow them
+      patch_tile(tile0, ws.ent[st], p.pool.arena + offk, cntk, ek, lane, p.err);
       __syncwarp();
 
       // ---- S^T = K . Q^T  (16 tokens x 8 head columns), two accumulator chains
@@ -583,7 +586,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
         }
       }
       __syncwarp();
-      patch_tile(tile0, ws.ent[st][1], p.pool.arena + offv, cntv, lane, p.err);
+      patch_tile(tile0, ws.ent[st] + ek, p.pool.arena + offv, cntv, stage_v(ek, cntv), lane, p.err);
       __syncwarp();
 
       // ---- O^T += V^T . P^T  (128 channels x 8 head columns)
