@@ -12,7 +12,31 @@
 
 namespace hx {
 
-constexpr int kBins = 4096;  // first-level histogram: top 12 bits of the key
+constexpr int kBins = 4096;  // histogram bins per level
+
+// Histogram bins are taken relative to an anchor: the order key of the score
+// of the (sequence, head)'s first page after its sinks. Level 1 bins are 2^16
+// key units wide (1/128 of an octave of score) and centred on the anchor, so
+// a row's scores spread over many bins whatever their magnitude; the two end
+// bins take everything more than 16 octaves away. Level 2 splits a level-1
+// bin into 4096 bins of 16 key units. Both are monotonic in the key.
+HX_DEVINL int64_t bin_rel(uint32_t key, uint32_t anchor) {
+  return (int64_t)key - (int64_t)anchor + ((int64_t)(kBins / 2) << 16);
+}
+HX_DEVINL int bin1(uint32_t key, uint32_t anchor) {
+  const int64_t e = bin_rel(key, anchor);
+  return e < 0 ? 0 : (int)min(e >> 16, (int64_t)(kBins - 1));
+}
+HX_DEVINL int bin2(uint32_t key, uint32_t anchor) { return (int)((bin_rel(key, anchor) >> 4) & (kBins - 1)); }
+HX_DEVINL bool edge_bin(int b) { return b == 0 || b == kBins - 1; }
+// Smallest 64-bit page key of level-1 bin b1 (level-2 bin b2 < 0: whole bin):
+// a page is in bins >= there iff its key64 >= the returned value.
+HX_DEVINL uint64_t bin_floor(int b1, int b2, uint32_t anchor) {
+  if (b1 == 0 && b2 < 0) return 0ull;
+  int64_t lo = (int64_t)anchor + ((int64_t)(b1 - kBins / 2) << 16) + (b2 > 0 ? 16ll * b2 : 0ll);
+  lo = lo < 0 ? 0 : (lo > 0xFFFFFFFFll ? 0xFFFFFFFFll : lo);
+  return (uint64_t)lo << 32;
+}
 
 // ---------------------------------------------------------------------------
 // compute_page_stats
@@ -79,7 +103,7 @@ __global__ void __launch_bounds__(256) quest_scores_kernel(const uint16_t* __res
                                                            int64_t head_stride, const int32_t* __restrict__ bt,
                                                            int bt_stride, const int32_t* __restrict__ seq_lens,
                                                            int S, int max_pages, int sinks_req, int pages_per_block,
-                                                           float* __restrict__ scores, uint32_t* __restrict__ hist) {
+                                                           float* __restrict__ scores) {
   __shared__ float s_qp[32 * V], s_qn[32 * V];
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh % H;
@@ -91,7 +115,6 @@ __global__ void __launch_bounds__(256) quest_scores_kernel(const uint16_t* __res
   }
   __syncthreads();
   const int n = (seq_lens[b] + S - 1) / S;
-  const int sinks = min(max(sinks_req, 0), n);
   const int lane = lane_id(), warp = threadIdx.x >> 5;
   const int j0 = blockIdx.x * pages_per_block;
   const int j1 = min(j0 + pages_per_block, min(n, max_pages));
@@ -131,10 +154,7 @@ __global__ void __launch_bounds__(256) quest_scores_kernel(const uint16_t* __res
     }
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-    if (lane == 0) {
-      scores[(int64_t)bh * max_pages + j] = acc;
-      if (hist && j >= sinks) atomicAdd(&hist[(int64_t)bh * 2 * kBins + (order_key(acc) >> 20)], 1u);
-    }
+    if (lane == 0) scores[(int64_t)bh * max_pages + j] = acc;
   }
 }
 
@@ -150,10 +170,8 @@ __global__ void __launch_bounds__(256) quest_scores_d128_kernel(const uint16_t* 
                                                                 const int32_t* __restrict__ bt, int bt_stride,
                                                                 const int32_t* __restrict__ seq_lens, int S,
                                                                 int max_pages, int sinks_req,
-                                                                float* __restrict__ scores,
-                                                                uint32_t* __restrict__ hist) {
+                                                                float* __restrict__ scores) {
   __shared__ float s_qp[128], s_qn[128];
-  __shared__ uint32_t s_hist[kBins];  // block-local histogram, flushed once
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh % H;
   if (threadIdx.x < 128) {
@@ -162,11 +180,8 @@ __global__ void __launch_bounds__(256) quest_scores_d128_kernel(const uint16_t* 
     s_qp[threadIdx.x] = qp;
     s_qn[threadIdx.x] = qn;
   }
-  if (hist)
-    for (int i = threadIdx.x; i < kBins; i += blockDim.x) s_hist[i] = 0;
   __syncthreads();
   const int n = min((seq_lens[b] + S - 1) / S, max_pages);
-  const int sinks = min(max(sinks_req, 0), n);
   const int lane = lane_id(), warp = threadIdx.x >> 5;
   const int base = blockIdx.x * 256 + warp * 32;
   if (base < n) {
@@ -221,17 +236,7 @@ __global__ void __launch_bounds__(256) quest_scores_d128_kernel(const uint16_t* 
       }
     }
     const int j = base + lane;
-    if (j < n) {
-      scores[(int64_t)bh * max_pages + j] = part[0];
-      if (hist && j >= sinks) atomicAdd(&s_hist[order_key(part[0]) >> 20], 1u);
-    }
-  }
-  if (hist) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
-      const uint32_t c = s_hist[i];
-      if (c) atomicAdd(&hist[(int64_t)bh * 2 * kBins + i], c);
-    }
+    if (j < n) scores[(int64_t)bh * max_pages + j] = part[0];
   }
 }
 
@@ -247,10 +252,37 @@ __global__ void __launch_bounds__(256) quest_scores_d128_kernel(const uint16_t* 
 constexpr int kQW = 16;      // warps per block
 constexpr int kQPB = 8;      // pages per batch
 constexpr int kQStages = 3;  // batches in smem per warp (2 in flight while one is scored)
+constexpr int kQHistRows = 2;  // (b, h) rows a block counts in smem
 struct __align__(128) QuestSmem {
   uint16_t rec[kQW][kQStages][kQPB][256];  // [warp][stage][page][min 128 | max 128]
+  uint32_t hist[kQHistRows][kBins];        // level-1 counts of the block's first two rows
   uint64_t bar[kQW][kQStages];
 };
+
+// Order key of page a's score (fp16 stats, D = 128, min row then max row),
+// by the same arithmetic as the batched scoring; lane l holds channels
+// 4l .. 4l+3 of the group terms.
+HX_DEVINL uint32_t anchor_key_d128(const uint16_t* __restrict__ kmin, int64_t page_stride, int64_t head_stride,
+                                   const int32_t* __restrict__ bt, int bt_stride, int b, int h, int a,
+                                   const float* qp, const float* qn, int lane) {
+  const int64_t phys = bt ? (int64_t)bt[(int64_t)b * bt_stride + a] : (int64_t)a;
+  const uint16_t* pm = kmin + phys * page_stride + (int64_t)h * head_stride;
+  const uint2 c = *reinterpret_cast<const uint2*>(pm + 4 * lane);
+  const uint2 x = *reinterpret_cast<const uint2*>(pm + 128 + 4 * lane);
+  const uint16_t xa[4] = {(uint16_t)(x.x & 0xffff), (uint16_t)(x.x >> 16), (uint16_t)(x.y & 0xffff),
+                          (uint16_t)(x.y >> 16)};
+  const uint16_t xc[4] = {(uint16_t)(c.x & 0xffff), (uint16_t)(c.x >> 16), (uint16_t)(c.y & 0xffff),
+                          (uint16_t)(c.y >> 16)};
+  float acc = 0.0f;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    acc = __fadd_rn(acc, __fmul_rn(qp[v], h2f(xa[v])));
+    acc = __fadd_rn(acc, __fmul_rn(qn[v], h2f(xc[v])));
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+  return order_key(acc);
+}
 
 // group_terms for channels 4 lane .. 4 lane + 3 (D = 128): one 8-byte load
 // per query head, the same per-channel arithmetic.
@@ -300,6 +332,8 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     for (int st = 0; st < kQStages; ++st) mbar_init(&sm.bar[warp][st], 1);
     fence_mbar_init();
   }
+  if (hist)
+    for (int i = threadIdx.x; i < kQHistRows * kBins; i += blockDim.x) (&sm.hist[0][0])[i] = 0;
   __syncthreads();
 
   // A warp takes a contiguous run of batches (so it rarely changes (b, h)):
@@ -356,6 +390,8 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
 
   const int64_t per = (total + nw - 1) / nw;
   const int64_t g0 = gw * per;
+  // the block's batches are contiguous: its first rows are counted in smem
+  const int bh0 = (int)min((int64_t)blockIdx.x * kQW * per, total) / nb;
   const int nk = (int)max((int64_t)0, min(per, total - g0));
   Bat p0 = {0, 0, 0, 0, 0}, p1 = {0, 0, 0, 0, 0}, p2 = {0, 0, 0, 0, 0};
   if (nk > 0) p0 = plan_next(true, g0);
@@ -364,7 +400,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   issue(p0, 0);
   issue(p1, 1 % kQStages);
   int cur_bh = -1;
-  uint32_t phase = 0;
+  uint32_t phase = 0, anchor = 0;
   bool dead = false;
   float qp[4], qn[4];
   for (int k = 0; k < nk; ++k) {
@@ -379,6 +415,12 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
       if (cb.bh != cur_bh) {
         const int b = cb.bh / H, h = cb.bh % H;
         group_terms4(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, mode, lane, qp, qn);
+        if (hist) {  // the row's anchor: page `sinks`, when there is one
+          const int n = min((seq_lens[b] + S - 1) / S, max_pages);
+          anchor = cb.sinks < n
+                       ? anchor_key_d128(kmin, page_stride, head_stride, bt, bt_stride, b, h, cb.sinks, qp, qn, lane)
+                       : 0u;
+        }
         cur_bh = cb.bh;
       }
       if (!dead && !mbar_wait(&sm.bar[warp][st], (phase >> st) & 1u)) {
@@ -420,15 +462,19 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
       const bool own = (lane & 3) == 0 && u < cb.cnt;
       if (own) scores[(int64_t)cb.bh * max_pages + j] = part[0];
       if (hist) {
-        // a (b, h)'s scores crowd into a few bins: pages of the batch that
-        // share a bin go as one atomic, or the same-address atomics serialise
+        // pages of the batch that share a bin go as one atomic; the block's
+        // first rows count in smem (flushed once at the end), any later row
+        // in global memory
         const bool counted = own && j >= cb.sinks;
-        const uint32_t bin = order_key(part[0]) >> 20;
+        const uint32_t bin = (uint32_t)bin1(order_key(part[0]), anchor);
         const uint32_t act = __ballot_sync(0xffffffffu, counted);
         if (counted) {
           const uint32_t peers = __match_any_sync(act, bin);
-          if (lane == __ffs(peers) - 1)
-            atomicAdd(&hist[(int64_t)cb.bh * 2 * kBins + bin], (uint32_t)__popc(peers));
+          const int row = cb.bh - bh0;
+          if (lane == __ffs(peers) - 1) {
+            if (row < kQHistRows) atomicAdd(&sm.hist[row][bin], (uint32_t)__popc(peers));
+            else atomicAdd(&hist[(int64_t)cb.bh * 2 * kBins + bin], (uint32_t)__popc(peers));
+          }
         }
       }
     }
@@ -437,18 +483,28 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     p1 = p2;
     p2 = p3;
   }
+  if (hist) {  // flush the smem counts: one atomic per nonzero bin
+    __syncthreads();
+    for (int i = threadIdx.x; i < kQHistRows * kBins; i += blockDim.x) {
+      const int row = i / kBins, bh = bh0 + row;
+      const uint32_t c = (&sm.hist[0][0])[i];
+      if (c && bh < B * H) atomicAdd(&hist[(int64_t)bh * 2 * kBins + (i % kBins)], c);
+    }
+  }
 }
 
-// Histogram of given scores (for the API path where scores come from outside).
+// Level-1 histogram of given scores (scores from outside, or from the scoring
+// kernels that do not count as they go).
 __global__ void quest_hist_kernel(const float* scores, int H, const int32_t* seq_lens, int S, int max_pages,
                                   int sinks_req, uint32_t* hist) {
   const int bh = blockIdx.y;
   const int b = bh / H;
   const int n = min((seq_lens[b] + S - 1) / S, max_pages);
   const int sinks = min(max(sinks_req, 0), n);
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
-    if (j >= sinks)
-      atomicAdd(&hist[(int64_t)bh * 2 * kBins + (order_key(scores[(int64_t)bh * max_pages + j]) >> 20)], 1u);
+  if (sinks >= n) return;
+  const uint32_t anchor = order_key(scores[(int64_t)bh * max_pages + sinks]);
+  for (int j = sinks + blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+    atomicAdd(&hist[(int64_t)bh * 2 * kBins + bin1(order_key(scores[(int64_t)bh * max_pages + j]), anchor)], 1u);
 }
 
 // ---------------------------------------------------------------------------
@@ -535,7 +591,7 @@ HX_DEVINL int find_boundary(const uint32_t* s_hist, uint32_t need, uint32_t& abo
 template <bool kGlobal>
 HX_DEVINL uint64_t radix_select(const uint64_t* cand, uint32_t cnt, uint32_t r, uint64_t prefix, int shift,
                                 uint32_t* s_h, uint32_t* s_warp, int* s_res) {
-  uint64_t mask = ~((1ull << shift) - 1ull);
+  uint64_t mask = shift >= 64 ? 0ull : ~((1ull << shift) - 1ull);
   while (shift > 0) {
     const int width = shift >= 8 ? 8 : shift;
     shift -= width;
@@ -578,10 +634,13 @@ HX_DEVINL void load_hist(uint32_t* s_hist, const uint32_t* g) {
   for (int u = 0; u < 4; ++u) reinterpret_cast<uint4*>(s_hist)[u * 256 + threadIdx.x] = v[u];
 }
 
-// hist layout per (b, h): [level 1: 4096 bins of key32 >> 20 | level 2: 4096
-// bins of key32 bits 19..8 among the level-1 boundary bin's pages]. The last
-// block gathers the keys of the level-2 boundary bin (a handful) into smem
-// and finishes the radix select there.
+// hist layout per (b, h): [level 1: 4096 anchored bins (bin1) of the non-sink
+// pages | level 2: 4096 bins (bin2) of the level-1 boundary bin's pages]. Every
+// block finds the level-1 boundary bin b*, then counts its slice's pages in
+// b* into level 2 and hands them to the last block as candidates; the last
+// block finds the level-2 boundary bin and ranks its keys (a handful). The
+// clamped end bins are not split by level 2: a boundary there is settled by
+// an exact radix select over all of the bin's keys.
 constexpr int kCandSmem = 1024;
 __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __restrict__ scores, int H,
                                                               const int32_t* __restrict__ seq_lens, int S,
@@ -606,10 +665,11 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
   const int n_ns = pl.n - pl.sinks;
 
   int bstar = -1;
-  uint32_t above = 0, r = 0;
+  uint32_t above = 0, r = 0, anchor = 0;
   bool full_bin = false;
   const bool trivial = (pl.k_eff == 0) || (pl.k_eff >= n_ns);
   if (!trivial) {
+    anchor = order_key(scores[(int64_t)bh * max_pages + pl.sinks]);
     load_hist(s_hist, hist_bh);
     __syncthreads();
     bstar = find_boundary(s_hist, (uint32_t)pl.k_eff, above, s_warp, s_res);
@@ -618,6 +678,7 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
     if (bstar >= 0 && !full_bin) {
       // this block's candidates of bin b*, with their level-2 histogram:
       // staged in smem, then one global reservation for the block
+      const bool split2 = !edge_bin(bstar);
       const int per = (n_ns + C - 1) / C;
       const int a = pl.sinks + blockIdx.x * per;
       const int e = min(a + per, pl.n);
@@ -635,12 +696,12 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
           const int j = base + u * blockDim.x + threadIdx.x;
           if (j < e) {
             const uint32_t k32 = order_key(v[u]);
-            if ((int)(k32 >> 20) == bstar) {
+            if (bin1(k32, anchor) == bstar) {
               const uint64_t key = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
               const uint32_t at = atomicAdd(&s_nc, 1u);
               if (at < (uint32_t)kCandSmem) s_cand[at] = key;
               else cand_bh[atomicAdd(&ctr[0], 1u)] = key;  // a slice past kCandSmem hits (long sequences)
-              atomicAdd(&hist2_bh[(k32 >> 8) & (kBins - 1)], 1u);
+              if (split2) atomicAdd(&hist2_bh[bin2(k32, anchor)], 1u);
             }
           }
         }
@@ -670,59 +731,64 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
     T = 0ull;
     if (threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
   } else if (full_bin) {
-    T = (uint64_t)bstar << 52;
+    T = bin_floor(bstar, -1, anchor);
   } else {
     const uint32_t cnt = *((volatile uint32_t*)&ctr[0]);
-    load_hist(s_hist, hist2_bh);
-    __syncthreads();
-    uint32_t above2;
-    const int b2 = find_boundary(s_hist, r, above2, s_warp, s_res);
-    if (b2 < 0) {
-      T = (uint64_t)bstar << 52;
-      if (threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
+    if (edge_bin(bstar)) {
+      T = radix_select<true>(cand_bh, cnt, r, 0ull, 64, s_h2, s_warp, s_res);
     } else {
-      const uint32_t r2 = r - above2;
-      const uint64_t pre = ((uint64_t)bstar << 52) | ((uint64_t)b2 << 40);
-      if (s_hist[b2] == r2) {
-        T = pre;
+      load_hist(s_hist, hist2_bh);
+      __syncthreads();
+      uint32_t above2;
+      const int b2 = find_boundary(s_hist, r, above2, s_warp, s_res);
+      if (b2 < 0) {
+        T = bin_floor(bstar, -1, anchor);
+        if (threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
       } else {
-        // gather the level-2 boundary bin's keys into smem and select there
-        if (threadIdx.x == 0) s_nc = 0;
-        __syncthreads();
-        for (uint32_t i0 = 0; i0 < cnt; i0 += 16 * blockDim.x) {
-          uint64_t key[16];
+        const uint32_t r2 = r - above2;
+        if (s_hist[b2] == r2) {
+          T = bin_floor(bstar, b2, anchor);
+        } else {
+          // gather the level-2 boundary bin's keys into smem and rank them
+          if (threadIdx.x == 0) s_nc = 0;
+          __syncthreads();
+          for (uint32_t i0 = 0; i0 < cnt; i0 += 16 * blockDim.x) {
+            uint64_t key[16];
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const uint32_t i = i0 + u * blockDim.x + threadIdx.x;
-            key[u] = i < cnt ? __ldcg(cand_bh + i) : 0ull;
-          }
+            for (int u = 0; u < 16; ++u) {
+              const uint32_t i = i0 + u * blockDim.x + threadIdx.x;
+              key[u] = i < cnt ? __ldcg(cand_bh + i) : 0ull;
+            }
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            if (i0 + u * blockDim.x + threadIdx.x < cnt && (key[u] >> 40) == (pre >> 40)) {
-              const uint32_t at = atomicAdd(&s_nc, 1u);
-              if (at < (uint32_t)kCandSmem) s_cand[at] = key[u];
+            for (int u = 0; u < 16; ++u) {
+              if (i0 + u * blockDim.x + threadIdx.x < cnt && bin2((uint32_t)(key[u] >> 32), anchor) == b2) {
+                const uint32_t at = atomicAdd(&s_nc, 1u);
+                if (at < (uint32_t)kCandSmem) s_cand[at] = key[u];
+              }
             }
           }
-        }
-        __syncthreads();
-        const uint32_t nc = s_nc;
-        if (nc <= blockDim.x) {
-          // a handful of keys: key i is T when exactly r2 - 1 keys beat it
-          if (threadIdx.x == 0) s_res[0] = -1;
           __syncthreads();
-          if (threadIdx.x < nc) {
-            const uint64_t mine = s_cand[threadIdx.x];
-            uint32_t beat = 0;
-            for (uint32_t i = 0; i < nc; ++i) beat += s_cand[i] > mine;
-            if (beat + 1 == r2) s_res[0] = (int)threadIdx.x;
+          const uint32_t nc = s_nc;
+          if (nc <= blockDim.x) {
+            // a handful of keys: key i is T when exactly r2 - 1 keys beat it
+            if (threadIdx.x == 0) s_res[0] = -1;
+            __syncthreads();
+            if (threadIdx.x < nc) {
+              const uint64_t mine = s_cand[threadIdx.x];
+              uint32_t beat = 0;
+              for (uint32_t i = 0; i < nc; ++i) beat += s_cand[i] > mine;
+              if (beat + 1 == r2) s_res[0] = (int)threadIdx.x;
+            }
+            __syncthreads();
+            const int w = s_res[0];
+            T = w >= 0 ? s_cand[w] : bin_floor(bstar, b2, anchor);
+            if (w < 0 && threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
+          } else if (nc <= (uint32_t)kCandSmem) {
+            T = radix_select<false>(s_cand, nc, r2, 0ull, 64, s_h2, s_warp, s_res);
+          } else {
+            // more than kCandSmem keys within 16 units of key: rank the whole bin
+            T = radix_select<true>(cand_bh, cnt, r, 0ull, 64, s_h2, s_warp, s_res);
           }
-          __syncthreads();
-          const int w = s_res[0];
-          T = w >= 0 ? s_cand[w] : pre;
-          if (w < 0 && threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
-        } else {
-          T = nc <= (uint32_t)kCandSmem ? radix_select<false>(s_cand, nc, r2, pre, 40, s_h2, s_warp, s_res)
-                                        : radix_select<true>(cand_bh, cnt, r2, pre, 40, s_h2, s_warp, s_res);
         }
       }
     }
@@ -931,7 +997,7 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
 #define HX_SC(TS_, V_)                                                                                      \
   quest_scores_kernel<TS_, V_><<<grid, 256, 0, s>>>(q, H, group, D, gqa_mode, (const TS_*)kmin, (const TS_*)kmax, \
                                                     page_stride, head_stride, block_table, bt_stride, seq_lens,    \
-                                                    page_size, max_pages, sink_pages, ppb, scores, hist)
+                                                    page_size, max_pages, sink_pages, ppb, scores)
   bool aligned = (((uintptr_t)kmin | (uintptr_t)kmax) & 7) == 0 && page_stride % 4 == 0 && head_stride % 4 == 0;
   if (stats_dtype == 1 && D == 128 && aligned && head_stride % 8 == 0 && page_stride % 8 == 0 &&
       ((uintptr_t)kmin & 15) == 0 && (const uint16_t*)kmax == (const uint16_t*)kmin + 128) {
@@ -957,11 +1023,8 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
     dim3 g2((max_pages + 255) / 256, B * H);
     quest_scores_d128_kernel<<<g2, 256, 0, s>>>(q, H, group, gqa_mode, (const uint16_t*)kmin, (const uint16_t*)kmax,
                                                 page_stride, head_stride, block_table, bt_stride, seq_lens, page_size,
-                                                max_pages, sink_pages, scores, hist);
-    HX_LAUNCH_CHECK();
-    return HX_OK;
-  }
-  if (stats_dtype == 1) {
+                                                max_pages, sink_pages, scores);
+  } else if (stats_dtype == 1) {
     if (V == 4 && D == 128 && !aligned) return HX_ERR_ARG;
     if (V == 1) HX_SC(uint16_t, 1);
     else if (V == 2) HX_SC(uint16_t, 2);
@@ -975,6 +1038,12 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
   }
 #undef HX_SC
   HX_LAUNCH_CHECK();
+  if (hist) {  // these kernels do not count as they go
+    dim3 hg((max_pages + 255) / 256 < 64 ? (max_pages + 255) / 256 : 64, B * H);
+    if (hg.x == 0) hg.x = 1;
+    quest_hist_kernel<<<hg, 256, 0, s>>>(scores, H, seq_lens, page_size, max_pages, sink_pages, hist);
+    HX_LAUNCH_CHECK();
+  }
   return HX_OK;
 }
 

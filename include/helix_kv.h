@@ -169,12 +169,11 @@ HX_API int hx_page_stats(void* stream, int32_t dtype, const void* k_pages,
  *   kmin + phys*page_stride + h*head_stride (same for kmax), phys =
  *   block_table ? block_table[b*bt_stride + j] : j,
  * with dtype 0 fp32 / 1 fp16. q is (B, H*group, D) fp16. Scores (B, H,
- * max_pages) fp32. If hist != NULL, the top 12 bits of each non-sink page's
- * order key are counted into hist (B*H, 2, 4096) [level 1; level 2 is used by
- * hx_quest_threshold], which must be zero on entry (hx_quest_threshold
- * leaves it zero again). On the fp16 D = 128 pool-layout path the first two
- * level-2 words of (b, h) = (0, 0) serve as work counters during the call and
- * are zero again when it ends.
+ * max_pages) fp32. If hist != NULL, each non-sink page is counted into
+ * hist (B*H, 2, 4096) [level 1; level 2 is used by hx_quest_threshold] at bin
+ * clamp((key - anchor) / 2^16 + 2048, 0, 4095), key = the order key of its
+ * score and anchor = that of page sinks (the first non-sink page). hist must
+ * be zero on entry (hx_quest_threshold leaves it zero again).
  * Replaces page_upper_bound / page_upper_bound_triton (reference.py:59-93,
  * triton_kernels.py:26-91) and the GQA contraction (compact_backend.py:231).
  */

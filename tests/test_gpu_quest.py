@@ -171,3 +171,28 @@ def test_select_top_blocks_for_layer_planted_block_and_sinks():
     ids, _ = select_top_blocks_for_layer(pool2, 0, q, used, BS, top_k=1, sink_blocks=2)
     assert {0, 1} <= set(ids.tolist())
     pool.check()
+
+
+@pytest.mark.parametrize("case", ["wide", "anchor_low", "anchor_high", "dup_wide", "negative"])
+def test_threshold_anchored_bins_wide_ranges(case):
+    """The histogram bins are centred on the first non-sink page's score and
+    clamp beyond 16 octaves; scores far from it (or a boundary inside a
+    clamped end bin) must still give the exact top-k."""
+    import quest
+    P, H, sinks, k = 20000, 3, 4, 5003
+    rng = np.random.default_rng({"wide": 1, "anchor_low": 2, "anchor_high": 3, "dup_wide": 4, "negative": 5}[case])
+    if case == "wide":         # log-uniform over 200 octaves, both signs
+        b = np.sign(rng.standard_normal((P, H))) * np.exp2(rng.uniform(-100, 100, (P, H)))
+    elif case == "anchor_low":  # every other score far above the anchor: top end bin
+        b = rng.uniform(1.0, 2.0, (P, H))
+        b[sinks] = 1e-30
+    elif case == "anchor_high":  # every other score far below the anchor: bottom end bin
+        b = rng.uniform(1.0, 2.0, (P, H))
+        b[sinks] = 1e30
+    elif case == "dup_wide":    # few distinct values spread wide, many ties
+        b = np.exp2(rng.integers(-60, 60, (P, H)).astype(np.float64))
+    else:                       # all negative, narrow
+        b = -rng.uniform(3.0, 3.001, (P, H))
+    b = b.astype(np.float32)
+    got = np16(quest.topk_pages_with_sinks(torch.from_numpy(b).cuda(), k, sinks))
+    np.testing.assert_array_equal(got, oq.topk_pages_with_sinks(b, k, sinks))
