@@ -224,6 +224,7 @@ def build_world(args, rank, world, device):
 def make_step(W, world, group, timing=None):
     """The decode step over all layers; `timing` records events around each kernel group."""
     import torch
+    import hxlib
     from kvquant import fused
     from kvquant.splitkv import exchange_partials
 
@@ -232,8 +233,8 @@ def make_step(W, world, group, timing=None):
     dev = pool.device
     scores = [torch.empty((1, H, shard.n_pages), dtype=torch.float32, device=dev) for _ in range(L)]
     thresh = [torch.empty((H,), dtype=torch.int64, device=dev) for _ in range(L)]
-    lists = [(torch.empty((H, shard.n_pages), dtype=torch.int32, device=dev),
-              torch.empty((H,), dtype=torch.int32, device=dev)) for _ in range(L)]
+    nsl = int(hxlib.lib().hx_quest_slices(shard.n_pages))
+    slices = [torch.empty((H, nsl + 1), dtype=torch.int32, device=dev) for _ in range(L)]
     o_loc = torch.empty((L, 1, H * G, D), dtype=torch.float32, device=dev)
     lse_loc = torch.empty((L, 1, H * G), dtype=torch.float32, device=dev)
     o_out = torch.empty((L, H * G, D), dtype=torch.float32, device=dev)
@@ -244,7 +245,7 @@ def make_step(W, world, group, timing=None):
             if timing is not None:
                 timing["ev"][li][0].record()
             sel = fused.quest_select(pool, li, q_all[li], bt, sl, top_k=W["k"], sink_pages=shard.sink_pages,
-                                     scores=scores[li], thresh=thresh[li], list_out=lists[li])
+                                     scores=scores[li], thresh=thresh[li], slice_out=slices[li])
             if timing is not None:
                 timing["ev"][li][1].record()
             fused.decode(pool, li, q_all[li], bt, sl, sel, page_begin=shard.page_begin, n_splits=W["ns"],
@@ -293,8 +294,9 @@ def run_ours(args):
     torch.cuda.synchronize()
     launches_per_step = hxlib.launch_count[0]
     graph = None
-    # collectives stay outside graphs this round: N > 1 times eager steps
-    use_graph = not args.no_graph and world == 1
+    # the whole step, the per-layer NCCL exchange included (the communicator
+    # exists from the warm-up steps), is captured once and replayed
+    use_graph = not args.no_graph
     if use_graph:
         try:
             graph = torch.cuda.CUDAGraph()
@@ -307,10 +309,16 @@ def run_ours(args):
             with torch.cuda.graph(graph):
                 step()
             torch.cuda.synchronize()
-        except Exception as e:  # capture not possible (e.g. collectives): eager replay
+        except Exception as e:  # capture not possible: eager replay
             graph = None
             use_graph = False
             print(f"[bench] graph capture failed, timing eager steps: {e}", file=sys.stderr)
+        if world > 1:  # every rank replays the graph or none does (same collectives on all ranks)
+            agree = torch.tensor([1 if use_graph else 0], dtype=torch.int32, device=device)
+            dist.all_reduce(agree, op=dist.ReduceOp.MIN)
+            if int(agree.item()) == 0:
+                graph = None
+                use_graph = False
     run = (lambda: graph.replay()) if graph is not None else step
     for _ in range(args.warmup):
         run()

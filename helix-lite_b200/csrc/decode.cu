@@ -80,6 +80,7 @@ struct __align__(256) CtaSmem {
   int32_t count;
   int32_t wcount[NW];
   int32_t last;
+  int32_t slice0, slice0_off;           // HX_SEL_SLICES: slice holding the CTA's first rank, its offset
 };
 
 // LUT dequant helpers. A table of 2-byte levels sits 256-aligned in smem; the
@@ -230,6 +231,13 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   const int NB = p.pool.num_blocks;
   const int seq_len = p.seq_lens[b];
   const int n = min((seq_len + DS - 1) / DS, p.max_pages);
+  // HX_SEL_SLICES: the row's slice offsets (exclusive selected counts of the
+  // slices of the non-sink pages), loaded first so the load overlaps the tables
+  const bool slices = p.sel_mode == HX_SEL_SLICES;
+  const int nsl = slices ? p.list_stride - 1 : 1;
+  const int32_t* soff = slices ? p.lists + (int64_t)bh * p.list_stride : nullptr;
+  const int32_t soff_lo = (slices && tid < nsl) ? soff[tid] : 0, soff_hi = (slices && tid < nsl) ? soff[tid + 1] : 0;
+  const int32_t soff_all = slices ? soff[nsl] : 0;
 
   // ---- per-CTA tables (all of a thread's loads in flight before its stores).
   // nuq4 K: channel d's 16 levels (32 B) at byte 32 d + 32 (d >> 5). nuq2 K:
@@ -318,14 +326,18 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   uint32_t inflight = 0;  // bit s = a bulk copy into stage s not yet waited for
   bool timed_out = false;
 
-  // ---- split range
+  // ---- split range (over the selected pages' ranks: sinks first, then the
+  // selected pages in ascending order)
+  const int sinks = min(max(p.sinks_req, 0), n);
+  const int sper = n > sinks ? (n - sinks + nsl - 1) / nsl : 1;
   int total;
   if (p.sel_mode == HX_SEL_LIST) total = min(p.list_counts[bh], p.list_stride);
+  else if (slices) total = min(sinks + max(soff_all, 0), n);
   else total = n;
   const int per = (total + p.n_splits - 1) / p.n_splits;
   const int ra = min(split * per, total), re = min(ra + per, total);
-  const int sinks = min(max(p.sinks_req, 0), n);
-  const uint64_t T = p.sel_mode == HX_SEL_THRESHOLD ? p.thresh[bh] : 0ull;
+  const uint64_t T = (p.sel_mode == HX_SEL_THRESHOLD || slices) ? p.thresh[bh] : 0ull;
+  int j_cur = -1, r_cur = 0;  // HX_SEL_SLICES scan cursor: page, non-sink rank of the next selected page
   const float* sc_bh = p.scores ? p.scores + (int64_t)bh * p.max_pages : nullptr;
   // a page whose 16 tokens all lie before t_cal gets its per-token V levels by
   // bulk copy with its codes when the rows are contiguous and 16-byte aligned
@@ -339,6 +351,64 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
 
   for (int rb = ra; rb < re; rb += LISTCAP) {
     const int rend = min(rb + LISTCAP, re);
+    if (slices) {
+      // the round's pages by rank: sinks are pages 0 .. sinks-1; the rest come
+      // from scanning the slices (4 pages a thread per pass) from the cursor
+      for (int r = rb + tid; r < rend; r += NT) sm.pages[r - rb] = r < sinks ? r : -1;
+      const int nb = max(rb, sinks) - sinks, ne = rend - sinks, c0 = max(0, min(rend, sinks) - rb);
+      if (nb < ne) {
+        if (j_cur < 0) {  // the slice holding non-sink rank nb
+          if (tid == 0) {
+            sm.slice0 = 0;
+            sm.slice0_off = 0;
+          }
+          __syncthreads();
+          if (tid < nsl && soff_lo <= nb && nb < soff_hi) {
+            sm.slice0 = tid;
+            sm.slice0_off = soff_lo;
+          }
+          __syncthreads();
+          j_cur = sinks + sm.slice0 * sper;
+          r_cur = sm.slice0_off;
+        }
+        while (r_cur < ne && j_cur < n) {
+          const int jt = j_cur + 4 * tid;
+          bool f[4];
+          int c = 0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            f[u] = jt + u < n && order_key64(sc_bh[jt + u], (uint32_t)(jt + u)) >= T;
+            c += f[u] ? 1 : 0;
+          }
+          int incl = c;  // inclusive scan over the warp, then over the warps
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int x = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += x;
+          }
+          if (lane == 31) sm.wcount[warp] = incl;
+          __syncthreads();
+          int before = 0, tt = 0;
+          for (int w = 0; w < NW; ++w) {
+            const int v = sm.wcount[w];
+            before += w < warp ? v : 0;
+            tt += v;
+          }
+          int rank = r_cur + before + incl - c;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (f[u]) {
+              if (rank >= nb && rank < ne) sm.pages[c0 + rank - nb] = jt + u;
+              ++rank;
+            }
+          __syncthreads();  // wcount is reused by the next pass
+          if (r_cur + tt > ne) break;  // the next round starts inside this tile
+          r_cur += tt;
+          j_cur += 4 * NT;
+        }
+      }
+      __syncthreads();
+    }
     if (tid == 0) sm.count = 0;
     __syncthreads();
     // gather the round's selected pages (ascending) with their directory records
@@ -347,9 +417,10 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       int j = -1;
       bool sel = false;
       if (idx < rend) {
-        j = p.sel_mode == HX_SEL_LIST ? p.lists[(int64_t)bh * p.list_stride + idx] : idx;
+        j = p.sel_mode == HX_SEL_LIST ? p.lists[(int64_t)bh * p.list_stride + idx]
+                                      : (slices ? sm.pages[idx - rb] : idx);
         if (j < 0 || j >= n) {
-          if (p.sel_mode == HX_SEL_LIST) set_err(p.err, HX_DEV_ERR_BOUNDS);
+          if (p.sel_mode == HX_SEL_LIST || slices) set_err(p.err, HX_DEV_ERR_BOUNDS);
         } else if (p.sel_mode == HX_SEL_THRESHOLD) {
           sel = (j < sinks) || order_key64(sc_bh[j], (uint32_t)j) >= T;
         } else {
@@ -907,7 +978,9 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
   if (sc->levels_k > (1 << pool->bits_k) || sc->levels_v > (1 << pool->bits_v) || sc->t_cal < 1) return HX_ERR_ARG;
   if (sel_mode == HX_SEL_THRESHOLD && (!scores || !thresh)) return HX_ERR_ARG;
   if (sel_mode == HX_SEL_LIST && (!lists || !list_counts || list_stride <= 0)) return HX_ERR_ARG;
-  if (sel_mode < 0 || sel_mode > 2) return HX_ERR_ARG;
+  if (sel_mode == HX_SEL_SLICES && (!scores || !thresh || !lists || list_stride < 2 || list_stride > NT + 1))
+    return HX_ERR_ARG;
+  if (sel_mode < 0 || sel_mode > 3) return HX_ERR_ARG;
   if (block_table && bt_stride < max_pages) return HX_ERR_ARG;
   DecodeParams p;
   p.pool = *pool;

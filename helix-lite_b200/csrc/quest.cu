@@ -641,18 +641,32 @@ HX_DEVINL void load_hist(uint32_t* s_hist, const uint32_t* g) {
 // block finds the level-2 boundary bin and ranks its keys (a handful). The
 // clamped end bins are not split by level 2: a boundary there is settled by
 // an exact radix select over all of the bin's keys.
+//
+// With slice_off != NULL the non-sink pages [sinks, n) of a row are also cut
+// into C = gridDim.x slices of ceil((n - sinks) / C) pages (block s = slice
+// s) and slice_off (B*H, C + 1) receives the exclusive prefix of each slice's
+// selected count: every block counts its slice's pages above the boundary bin
+// (and, when the boundary bin is taken whole, in it), and the last block adds
+// the boundary candidates that pass the threshold.
 constexpr int kCandSmem = 1024;
+constexpr int kMaxSlices = 128;
+// threshold blocks (= slices) per row: one per 1024 pages, 1 .. kMaxSlices
+inline int quest_slices(int max_pages) {
+  const int c = (max_pages + 1023) / 1024;
+  return c < 1 ? 1 : (c > kMaxSlices ? kMaxSlices : c);
+}
 __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __restrict__ scores, int H,
                                                               const int32_t* __restrict__ seq_lens, int S,
                                                               int max_pages, int sinks_req, int k_fixed, int fnum,
                                                               int fden, uint32_t* hist, uint64_t* cand,
-                                                              uint32_t* counters, uint64_t* thresh, uint32_t* err) {
+                                                              uint32_t* counters, uint64_t* thresh,
+                                                              int32_t* slice_off, uint32_t* err) {
   __shared__ __align__(16) uint32_t s_hist[kBins];
   __shared__ uint32_t s_warp[8];
   __shared__ int s_res[4];
   __shared__ uint32_t s_h2[256];
   __shared__ uint64_t s_cand[kCandSmem];
-  __shared__ uint32_t s_nc;
+  __shared__ uint32_t s_nc, s_above;
   __shared__ int s_last;
   const int bh = blockIdx.y;
   const int b = bh / H;
@@ -675,14 +689,20 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
     bstar = find_boundary(s_hist, (uint32_t)pl.k_eff, above, s_warp, s_res);
     r = (uint32_t)pl.k_eff - above;
     full_bin = bstar >= 0 && s_hist[bstar] == r;
-    if (bstar >= 0 && !full_bin) {
+    if (bstar >= 0 && (!full_bin || slice_off)) {
       // this block's candidates of bin b*, with their level-2 histogram:
-      // staged in smem, then one global reservation for the block
+      // staged in smem, then one global reservation for the block (with
+      // slices: also the count of its pages above b*, or at / above it when
+      // b* is taken whole, in which case nothing else is gathered)
       const bool split2 = !edge_bin(bstar);
       const int per = (n_ns + C - 1) / C;
       const int a = pl.sinks + blockIdx.x * per;
       const int e = min(a + per, pl.n);
-      if (threadIdx.x == 0) s_nc = 0;
+      uint32_t my_above = 0;
+      if (threadIdx.x == 0) {
+        s_nc = 0;
+        s_above = 0;
+      }
       __syncthreads();
       for (int base = a; base < e; base += 4 * blockDim.x) {
         float v[4];
@@ -696,7 +716,9 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
           const int j = base + u * blockDim.x + threadIdx.x;
           if (j < e) {
             const uint32_t k32 = order_key(v[u]);
-            if (bin1(k32, anchor) == bstar) {
+            const int b1 = bin1(k32, anchor);
+            my_above += (b1 > bstar || (full_bin && b1 == bstar)) ? 1u : 0u;
+            if (b1 == bstar && !full_bin) {
               const uint64_t key = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
               const uint32_t at = atomicAdd(&s_nc, 1u);
               if (at < (uint32_t)kCandSmem) s_cand[at] = key;
@@ -706,12 +728,20 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
           }
         }
       }
+      if (slice_off) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) my_above += __shfl_xor_sync(0xffffffffu, my_above, o);
+        if ((threadIdx.x & 31) == 0 && my_above) atomicAdd(&s_above, my_above);
+      }
       __syncthreads();
+      if (slice_off && threadIdx.x == 0) slice_off[(int64_t)bh * (C + 1) + blockIdx.x] = (int32_t)s_above;
       const uint32_t nloc = min(s_nc, (uint32_t)kCandSmem);
-      if (threadIdx.x == 0) s_res[0] = (int)atomicAdd(&ctr[0], nloc);
-      __syncthreads();
-      const uint32_t gbase = (uint32_t)s_res[0];
-      for (uint32_t i = threadIdx.x; i < nloc; i += blockDim.x) cand_bh[gbase + i] = s_cand[i];
+      if (nloc) {
+        if (threadIdx.x == 0) s_res[0] = (int)atomicAdd(&ctr[0], nloc);
+        __syncthreads();
+        const uint32_t gbase = (uint32_t)s_res[0];
+        for (uint32_t i = threadIdx.x; i < nloc; i += blockDim.x) cand_bh[gbase + i] = s_cand[i];
+      }
       __syncthreads();
     }
   }
@@ -791,6 +821,41 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
           }
         }
       }
+    }
+  }
+  if (slice_off) {
+    // final selected count of every slice, then the exclusive prefix
+    uint32_t* s_add = s_h2;  // C <= kMaxSlices <= 256 counters
+    const int per = n_ns > 0 ? (n_ns + C - 1) / C : 1;
+    __syncthreads();
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+      uint32_t v;
+      if (pl.k_eff == 0) v = 0;
+      else if (pl.k_eff >= n_ns) v = (uint32_t)max(0, min(per, n_ns - i * per));  // every page
+      else if (bstar < 0) v = 0;
+      else v = (uint32_t)__ldcg(slice_off + (int64_t)bh * (C + 1) + i);
+      s_add[i] = v;
+    }
+    __syncthreads();
+    if (!trivial && bstar >= 0 && !full_bin) {
+      const uint32_t cnt = *((volatile uint32_t*)&ctr[0]);
+      for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+        const uint64_t key = __ldcg(cand_bh + i);
+        if (key >= T) {
+          const int j = (int)(~(uint32_t)key);
+          atomicAdd(&s_add[min((j - pl.sinks) / per, C - 1)], 1u);
+        }
+      }
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+      int32_t acc = 0;
+      for (int i = 0; i < C; ++i) {
+        const int32_t c = (int32_t)s_add[i];
+        slice_off[(int64_t)bh * (C + 1) + i] = acc;
+        acc += c;
+      }
+      slice_off[(int64_t)bh * (C + 1) + C] = acc;
     }
   }
   if (threadIdx.x == 0) {
@@ -1047,10 +1112,21 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
   return HX_OK;
 }
 
+HX_API int32_t hx_quest_slices(int32_t max_pages) { return quest_slices(max_pages); }
+
 HX_API int hx_quest_threshold(void* stream, const float* scores, int32_t B, int32_t H, const int32_t* seq_lens,
                               int32_t page_size, int32_t max_pages, int32_t sink_pages, int32_t k_fixed,
                               int32_t frac_num, int32_t frac_den, int32_t hist_ready, uint32_t* hist,
                               uint64_t* cand, uint32_t* counters, uint64_t* thresh, uint32_t* dev_err) {
+  return hx_quest_threshold_slices(stream, scores, B, H, seq_lens, page_size, max_pages, sink_pages, k_fixed,
+                                   frac_num, frac_den, hist_ready, hist, cand, counters, thresh, nullptr, dev_err);
+}
+
+HX_API int hx_quest_threshold_slices(void* stream, const float* scores, int32_t B, int32_t H,
+                                     const int32_t* seq_lens, int32_t page_size, int32_t max_pages,
+                                     int32_t sink_pages, int32_t k_fixed, int32_t frac_num, int32_t frac_den,
+                                     int32_t hist_ready, uint32_t* hist, uint64_t* cand, uint32_t* counters,
+                                     uint64_t* thresh, int32_t* slice_off, uint32_t* dev_err) {
   if (B < 0 || H <= 0 || page_size <= 0 || max_pages < 0 || frac_den < 0) return HX_ERR_ARG;
   if (B == 0) return HX_OK;
   if (!scores || !seq_lens || !hist || !cand || !counters || !thresh) return HX_ERR_ARG;
@@ -1060,12 +1136,10 @@ HX_API int hx_quest_threshold(void* stream, const float* scores, int32_t B, int3
     if (hg.x == 0) hg.x = 1;
     quest_hist_kernel<<<hg, 256, 0, st>>>(scores, H, seq_lens, page_size, max_pages, sink_pages, hist);
   }
-  int C = (max_pages + 1023) / 1024;
-  C = C < 1 ? 1 : (C > 128 ? 128 : C);
-  dim3 grid(C, B * H);
+  dim3 grid(quest_slices(max_pages), B * H);
   quest_threshold_kernel<<<grid, 256, 0, st>>>(scores, H, seq_lens, page_size, max_pages, sink_pages,
                                                        k_fixed, frac_num, frac_den, hist, cand, counters, thresh,
-                                                       dev_err);
+                                                       slice_off, dev_err);
   HX_LAUNCH_CHECK();
   return HX_OK;
 }

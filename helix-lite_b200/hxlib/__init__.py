@@ -20,7 +20,7 @@ LIB_PATH = Path(os.environ.get("HELIX_KV_LIB", _HERE / "libhelix_kv.so"))
 HX_OK, HX_ERR_ARG, HX_ERR_UNSUPPORTED, HX_ERR_LAUNCH, HX_ERR_SCRATCH_LIMIT = 0, 1, 2, 3, 4
 DEV_ERR = {0x1: "outlier arena full", 0x2: "index out of range", 0x4: "bounded wait ran out",
            0x8: "selection threshold not isolated"}
-SEL_DENSE, SEL_THRESHOLD, SEL_LIST = 0, 1, 2
+SEL_DENSE, SEL_THRESHOLD, SEL_LIST, SEL_SLICES = 0, 1, 2, 3
 
 c_vp, c_i32, c_i64, c_f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
 
@@ -55,6 +55,9 @@ _SIGS = {
                                 c_i64, c_vp, c_i32, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp]),
     "hx_quest_threshold": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32,
                                    c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "hx_quest_slices": (c_i32, [c_i32]),
+    "hx_quest_threshold_slices": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32,
+                                          c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "hx_quest_compact": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32,
                                  c_vp, c_vp]),
     "hx_quest_lists": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]),
@@ -101,7 +104,7 @@ def lib():
 # kernel launches each entry point makes (bench.py counts launches with this)
 LAUNCHES = {"hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 1, "hx_unpack_pages": 1,
             "hx_nuq_pack_dense": 1, "hx_nuq_unpack_dense": 1, "hx_nuq_quantize_flat": 2,
-            "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": 1,
+            "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": 1, "hx_quest_threshold_slices": 1,
             "hx_quest_compact": 1, "hx_quest_lists": 2, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_merge_partials": 1,
             "hx_selected_attention": 1}
 launch_count = [0]

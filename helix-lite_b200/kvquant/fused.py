@@ -12,10 +12,11 @@ fp16 staging buffer (src/kvquant/compact_backend.py:225-299):
                  normalised o (fp32) and lse (natural log)
   selected_lists the selection as ascending page lists (API / tests)
 
-quest_select also writes the selection as ascending per-(b, h) page lists
-(two bandwidth-bound passes over the scores), and decode balances its splits
-over those lists, so every CTA gets the same number of selected pages however
-the selection clusters along the sequence.
+quest_select also returns, per (b, h), how many pages each slice of the
+sequence contributes (the threshold kernel's blocks count them as they go),
+and decode balances its splits over the selected pages with them: every CTA
+gets the same number of selected pages however the selection clusters along
+the sequence, and finds its pages by scanning the scores of its slices.
 
 Everything is asynchronous on the current stream; scratch is cached per
 device and left zeroed by the kernels.
@@ -28,7 +29,7 @@ from dataclasses import dataclass
 import torch
 
 import hxlib
-from hxlib import SEL_DENSE, SEL_LIST, SEL_THRESHOLD, call, ptr, stream
+from hxlib import SEL_DENSE, SEL_LIST, SEL_SLICES, SEL_THRESHOLD, call, ptr, stream
 
 from .compact_pool import CompactKVPool, ctypes_ref
 
@@ -45,6 +46,7 @@ class Selection:
     sink_pages: int
     lists: torch.Tensor | None = None   # (B * H, max_pages) int32 ascending selected pages
     counts: torch.Tensor | None = None  # (B * H,) int32
+    slice_off: torch.Tensor | None = None  # (B * H, slices + 1) int32 exclusive selected counts
 
 
 def _i32(t, device):
@@ -54,8 +56,9 @@ def _i32(t, device):
 def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
                  seq_lens: torch.Tensor, *, top_k: int | None = None, top_frac=(1, 4), sink_pages: int = 4,
                  gqa: str = "sum", max_pages: int | None = None, scores: torch.Tensor | None = None,
-                 thresh: torch.Tensor | None = None, lists: bool = True,
-                 list_out: tuple[torch.Tensor, torch.Tensor] | None = None) -> Selection:
+                 thresh: torch.Tensor | None = None, lists: bool = False,
+                 list_out: tuple[torch.Tensor, torch.Tensor] | None = None,
+                 slice_out: torch.Tensor | None = None) -> Selection:
     """Score every page of each sequence and fix the exact top-K thresholds.
 
     query (B, Hq, D) fp16 with Hq = group * H; block_table (B, >= max_pages)
@@ -64,9 +67,11 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
     k = top_k pages if given,
     else floor(n_pages * top_frac[0] / top_frac[1]); gqa "sum" adds the
     per-query-head bounds of a group, "mean" bounds the group's mean query
-    (the reference hook, compact_backend.py:231). ``lists`` also writes the
-    ascending page lists the decode balances over, into ``list_out`` =
-    ((B*H, max_pages) int32, (B*H,) int32) when given.
+    (the reference hook, compact_backend.py:231). The per-slice counts the
+    decode balances over land in ``slice_out`` ((B*H, slices + 1) int32,
+    slices = hx_quest_slices(max_pages)) when given. ``lists`` also writes
+    the ascending page lists, into ``list_out`` = ((B*H, max_pages) int32,
+    (B*H,) int32) when given.
     """
     dev = pool.device
     q = query.to(device=dev, dtype=torch.float16).contiguous()
@@ -93,10 +98,15 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
              ptr(stats), hxlib.ctypes.c_void_p(stats.data_ptr() + 2 * D), 2 * D, pool.num_blocks * 2 * D,
              ptr(bt), bt.shape[1], ptr(sl), S, mp, sink_pages, ptr(scores), ptr(hist))
         kf, fn, fd = (int(top_k), 0, 0) if top_k is not None else (0, int(top_frac[0]), int(top_frac[1]))
-        call("hx_quest_threshold", st, ptr(scores), B, H, ptr(sl), S, mp, sink_pages, kf, fn, fd, 1, ptr(hist),
-             ptr(cand), ptr(ctr), ptr(thresh), ptr(hxlib.err_word(dev)))
+        nsl = int(hxlib.lib().hx_quest_slices(mp))
+        if slice_out is None:
+            slice_out = torch.empty((B * H, nsl + 1), dtype=torch.int32, device=dev)
+        if slice_out.shape != (B * H, nsl + 1) or slice_out.dtype != torch.int32:
+            raise ValueError(f"slice_out must be ({B * H}, {nsl + 1}) int32")
+        call("hx_quest_threshold_slices", st, ptr(scores), B, H, ptr(sl), S, mp, sink_pages, kf, fn, fd, 1,
+             ptr(hist), ptr(cand), ptr(ctr), ptr(thresh), ptr(slice_out), ptr(hxlib.err_word(dev)))
         lst = cnt = None
-        if lists:
+        if lists or list_out is not None:
             mpl = max(mp, 1)
             if list_out is not None:
                 lst, cnt = list_out
@@ -109,7 +119,7 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
             chunks = hxlib.scratch(dev, "quest_chunks", B * H * nch * 4)
             call("hx_quest_lists", st, ptr(scores), ptr(thresh), B, H, ptr(sl), S, mp, sink_pages, mpl, ptr(lst),
                  ptr(cnt), ptr(chunks))
-    return Selection(scores, thresh, sl, S, mp, sink_pages, lst, cnt)
+    return Selection(scores, thresh, sl, S, mp, sink_pages, lst, cnt, slice_out)
 
 
 def selected_lists(sel: Selection, union: bool = False, max_out: int | None = None):
@@ -142,10 +152,12 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
            o: torch.Tensor | None = None, lse: torch.Tensor | None = None):
     """Fused-dequant decode attention; returns (o (B, Hq, D) fp32, lse (B, Hq)).
 
-    Pages attended: every page (no selection), the Quest selection, or
-    explicit per-(b, h) logical page lists (``lists`` (B, H, L) int32 with
-    ``list_counts`` (B, H)). ``page_begin`` is the absolute logical page of
-    this pool's page 0 (split-KV shards), used for V's position clamp.
+    Pages attended: every page (no selection), the Quest selection (split
+    over its selected pages by the selection's slice counts, else by its
+    lists when it has them, else over the sequence), or explicit per-(b, h)
+    logical page lists (``lists`` (B, H, L) int32 with ``list_counts`` (B,
+    H)). ``page_begin`` is the absolute logical page of this pool's page 0
+    (split-KV shards), used for V's position clamp.
     """
     dev = pool.device
     q = query.to(device=dev, dtype=torch.float16).contiguous()
@@ -154,7 +166,12 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
     bt = _i32(block_table, dev)
     sl = _i32(seq_lens, dev)
     mp = int(max_pages if max_pages is not None else bt.shape[1])
-    if selection is not None and selection.lists is not None and lists is None:
+    slice_off = None
+    if selection is not None and selection.slice_off is not None and lists is None:
+        mp = selection.max_pages
+        slice_off = selection.slice_off
+        mode = SEL_SLICES
+    elif selection is not None and selection.lists is not None and lists is None:
         lists, list_counts = selection.lists, selection.counts
         mode = SEL_LIST
         selection = None
@@ -178,6 +195,9 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
         lists_c = _i32(lists, dev).view(B * H, -1)
         counts_c = _i32(list_counts, dev)
         lstride = lists_c.shape[1]
+    elif mode == SEL_SLICES:
+        lists_c, counts_c = slice_off, None
+        lstride = slice_off.shape[1]
     else:
         lists_c = counts_c = None
         lstride = 0

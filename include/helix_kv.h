@@ -200,6 +200,19 @@ HX_API int hx_quest_threshold(void* stream, const float* scores, int32_t B, int3
                               int32_t hist_ready, uint32_t* hist, uint64_t* cand, uint32_t* counters,
                               uint64_t* thresh, uint32_t* dev_err);
 
+/* hx_quest_threshold plus the per-slice counts the decode balances its splits
+ * over (HX_SEL_SLICES): the non-sink pages [sinks, n_b) of each (b, h) are
+ * cut into C = hx_quest_slices(max_pages) slices of ceil((n_b - sinks) / C)
+ * pages, and slice_off (B*H, C + 1) int32 receives the exclusive prefix of
+ * the slices' selected counts (slice_off[C] = selected non-sink pages). No
+ * reference counterpart (the reference hands FlashAttention a page list). */
+HX_API int32_t hx_quest_slices(int32_t max_pages);
+HX_API int hx_quest_threshold_slices(void* stream, const float* scores, int32_t B, int32_t H,
+                                     const int32_t* seq_lens, int32_t page_size, int32_t max_pages,
+                                     int32_t sink_pages, int32_t k_fixed, int32_t frac_num, int32_t frac_den,
+                                     int32_t hist_ready, uint32_t* hist, uint64_t* cand, uint32_t* counters,
+                                     uint64_t* thresh, int32_t* slice_off, uint32_t* dev_err);
+
 /* Selected logical pages, ascending, per (b, h): out (B, H, max_out) int32
  * and counts (B, H). union_heads != 0 writes the union over heads instead:
  * out (B, max_out), counts (B). */
@@ -227,6 +240,7 @@ HX_API int hx_quest_lists(void* stream, const float* scores, const uint64_t* thr
 #define HX_SEL_DENSE     0   /* every page of the sequence                  */
 #define HX_SEL_THRESHOLD 1   /* sinks + pages with key64 >= thresh          */
 #define HX_SEL_LIST      2   /* explicit per-(b, h) logical page lists      */
+#define HX_SEL_SLICES    3   /* sinks + key64 >= thresh, ranks located by slice_off */
 
 /* Scratch bytes hx_decode_attn needs for B sequences, H heads, n_splits. */
 HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits);
@@ -238,7 +252,10 @@ HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits);
  * (page_begin + j) * 16 (V tail clamp); tokens >= seq_lens[b] are masked.
  * Selection: HX_SEL_DENSE; HX_SEL_THRESHOLD with scores / thresh from
  * hx_quest_scores / hx_quest_threshold; HX_SEL_LIST with lists (B, H,
- * list_stride) and list_counts (B, H). The sequence is split n_splits ways
+ * list_stride) and list_counts (B, H); HX_SEL_SLICES with scores / thresh
+ * and slice_off from hx_quest_threshold_slices passed as lists, list_stride
+ * = C + 1 (list_counts unused): the splits balance over the selected pages
+ * as with lists, and each CTA finds its pages by scanning its slices. The sequence is split n_splits ways
  * per (b, h); the last CTA of each (b, h) merges the splits. Writes o (B,
  * H*group, D) fp32 normalised, lse (B, H*group) natural log (-inf for an
  * empty selection), and out16 (same shape, fp16) when non-NULL. scratch:

@@ -3,6 +3,7 @@ dequantise-then-attend on the oracle pool, within 2e-3 max-abs; and the
 cross-shard (o, lse) merge."""
 from __future__ import annotations
 
+import dataclasses
 import math
 
 import numpy as np
@@ -100,8 +101,8 @@ def test_quest_decode_matches_oracle_config3_shape():
     ro, rl = _oracle_out(orc, 0, q, bt, sl, [pages])
     assert np.abs(np16(o) - ro).max() < TOL
     np.testing.assert_allclose(np16(lse), rl, atol=1e-3)
-    # the same selection read from the thresholds instead of the lists
-    sel_t = fused.quest_select(gpu, 0, q, bt, sl, top_frac=(1, 4), sink_pages=4, lists=False)
+    # the same selection read from the thresholds alone (splits over the sequence)
+    sel_t = dataclasses.replace(sel, slice_off=None, lists=None, counts=None)
     o_t, lse_t = fused.decode(gpu, 0, q, bt, sl, sel_t)
     gpu.check()
     assert np.abs(np16(o_t) - ro).max() < TOL
@@ -209,3 +210,45 @@ def test_decode_scale_and_group_one():
     K, V = orc.dequant_sequence(0, np16(bt[0]), 700)
     ro, _ = oatt.decode_attention(np16(q[0]).astype(np.float64), K, V, scale=0.05)
     assert np.abs(np16(o[0]) - ro).max() < TOL
+
+
+@pytest.mark.parametrize("k,n_splits", [(None, 7), (0, 5), (3, 37), (100000, 11), (None, 160)])
+def test_decode_slice_counts_match_lists(k, n_splits):
+    """The decode balanced by the threshold's per-slice counts (HX_SEL_SLICES)
+    gives every CTA the same pages, in the same order, as the balanced lists
+    (HX_SEL_LIST): bit-identical outputs, within TOL of the oracle. Ragged
+    sequences (one shorter than the sinks), k = 0, k past every page, more
+    splits than selected pages, a clustered selection (a planted block)."""
+    from kvquant import fused
+    from kvquant.synthetic import NUQ2
+    lens = [40, 3 * 16 * 1024 + 9, 20000, 16 * 700]
+    gpu, orc, bt, sl = _build([NUQ2], lens, seed=60, B=len(lens), shuffle=True)
+    q = _query(len(lens), 7, 61)
+    st = gpu.layers[0].stats  # (H, NB, 2, D): plant high-bound pages in one block of sequence 1
+    rows = bt[1, 1000:1060].long()
+    st[:, rows, 1] = 30.0
+    kw = dict(top_k=k) if k is not None else dict(top_frac=(1, 4))
+    sel = fused.quest_select(gpu, 0, q, bt, sl, sink_pages=4, lists=True, **kw)
+    assert sel.slice_off is not None and sel.lists is not None
+    o_s, lse_s = fused.decode(gpu, 0, q, bt, sl, sel, n_splits=n_splits)
+    o_l, lse_l = fused.decode(gpu, 0, q, bt, sl, dataclasses.replace(sel, slice_off=None), n_splits=n_splits)
+    gpu.check()
+    np.testing.assert_array_equal(np16(o_s).view(np.uint32), np16(o_l).view(np.uint32))
+    np.testing.assert_array_equal(np16(lse_s).view(np.uint32), np16(lse_l).view(np.uint32))
+    # the slice counts themselves: selected non-sink pages of each slice
+    off = np16(sel.slice_off)
+    lists, counts = np16(sel.lists), np16(sel.counts)
+    nsl = off.shape[1] - 1
+    for b, n_tok in enumerate(lens):
+        n = -(-n_tok // 16)
+        sinks = min(4, n)
+        per = -(-(n - sinks) // nsl) if n > sinks else 1
+        for h in range(4):
+            row = b * 4 + h
+            pages = lists[row, :counts[row]]
+            rest = pages[pages >= sinks]
+            want = np.bincount(np.minimum((rest - sinks) // per, nsl - 1), minlength=nsl)
+            np.testing.assert_array_equal(np.diff(off[row]), want)
+    pages = [[lists[b * 4 + h, :counts[b * 4 + h]] for h in range(4)] for b in range(len(lens))]
+    ro, _ = _oracle_out(orc, 0, q, bt, sl, pages)
+    assert np.abs(np16(o_s) - ro).max() < TOL

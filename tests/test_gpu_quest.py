@@ -62,7 +62,7 @@ def test_selection_edge_sizes(P, k, sinks):
     q = torch.randn((1, H, D), device="cuda").to(torch.float16)
     bt = torch.arange(P, dtype=torch.int32, device="cuda").unsqueeze(0)
     sl = torch.tensor([P * 16 - 3], dtype=torch.int32, device="cuda")
-    sel = quest_select(pool, 0, q, bt, sl, top_k=k, sink_pages=sinks)
+    sel = quest_select(pool, 0, q, bt, sl, top_k=k, sink_pages=sinks, lists=True)
     lists, counts = selected_lists(sel)
     pool.check()
     qp, qn = oq.group_terms(np16(q[0]), 1, "sum")
@@ -102,7 +102,7 @@ def test_batched_selection_with_block_tables_and_union():
     bt = torch.stack([perm[:300], perm[300:]])                   # two sequences
     sl = torch.tensor([300 * 16, 250 * 16 - 7], dtype=torch.int32, device="cuda")
     q = torch.randn((2, H * 7, D), generator=g, device="cuda").to(torch.float16)
-    sel = quest_select(pool, 0, q, bt, sl, top_frac=(1, 4), sink_pages=4)
+    sel = quest_select(pool, 0, q, bt, sl, top_frac=(1, 4), sink_pages=4, lists=True)
     lists, counts = selected_lists(sel)
     ulists, ucounts = selected_lists(sel, union=True)
     pool.check()
