@@ -248,16 +248,15 @@ def make_step(W, world, group, timing=None):
                                      scores=scores[li], thresh=thresh[li], slice_out=slices[li])
             if timing is not None:
                 timing["ev"][li][1].record()
+            # one GPU: the decode writes the layer's output in place
             fused.decode(pool, li, q_all[li], bt, sl, sel, page_begin=shard.page_begin, n_splits=W["ns"],
-                         o=o_loc[li], lse=lse_loc[li])
+                         o=o_loc[li] if world > 1 else o_out[li].view(1, H * G, D), lse=lse_loc[li])
             if timing is not None:
                 timing["ev"][li][2].record()
             if world > 1:
                 O, Lz = exchange_partials(o_loc[li].view(H * G, D), lse_loc[li].view(H * G), group)
                 om, _ = fused.merge_partials(O, Lz)
                 o_out[li].copy_(om)
-            else:
-                o_out[li].copy_(o_loc[li, 0])
         return o_out
 
     return step

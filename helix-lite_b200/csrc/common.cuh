@@ -126,7 +126,34 @@ HX_DEVINL uint32_t pack_u16x2(uint16_t lo, uint16_t hi) {
   return (uint32_t)lo | ((uint32_t)hi << 16);
 }
 
+// ---- programmatic dependent launch ------------------------------------------
+// The step's kernels are launched so that the next one may start while this
+// one runs: pdl_allow_next() lets the next grid launch once every CTA of this
+// one has called it (or exited); pdl_wait() blocks until the previous grid in
+// the stream has completed and its writes are visible. Work before pdl_wait()
+// may touch only data no earlier kernel writes (this CTA's smem, calibration
+// tables). Both are no-ops for a grid launched without the attribute.
+HX_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+HX_DEVINL void pdl_allow_next() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 }  // namespace hx
+
+// Launch with programmatic stream serialisation (see pdl_wait).
+template <typename... KArgs, typename... Args>
+static inline cudaError_t hx_launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                        Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 // Host-side launch check shared by the C entry points.
 #define HX_LAUNCH_CHECK()                                   \

@@ -229,15 +229,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   const int G = p.G;
   const int Tc = p.sc.t_cal;
   const int NB = p.pool.num_blocks;
-  const int seq_len = p.seq_lens[b];
-  const int n = min((seq_len + DS - 1) / DS, p.max_pages);
-  // HX_SEL_SLICES: the row's slice offsets (exclusive selected counts of the
-  // slices of the non-sink pages), loaded first so the load overlaps the tables
-  const bool slices = p.sel_mode == HX_SEL_SLICES;
-  const int nsl = slices ? p.list_stride - 1 : 1;
-  const int32_t* soff = slices ? p.lists + (int64_t)bh * p.list_stride : nullptr;
-  const int32_t soff_lo = (slices && tid < nsl) ? soff[tid] : 0, soff_hi = (slices && tid < nsl) ? soff[tid + 1] : 0;
-  const int32_t soff_all = slices ? soff[nsl] : 0;
+  pdl_allow_next();
 
   // ---- per-CTA tables (all of a thread's loads in flight before its stores).
   // nuq4 K: channel d's 16 levels (32 B) at byte 32 d + 32 (d >> 5). nuq2 K:
@@ -284,6 +276,18 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
     for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
     fence_mbar_init();
   }
+  // everything above reads calibration tables only; from here on the inputs
+  // may come from the kernels before this one
+  pdl_wait();
+  const int seq_len = p.seq_lens[b];
+  const int n = min((seq_len + DS - 1) / DS, p.max_pages);
+  // HX_SEL_SLICES: the row's slice offsets (exclusive selected counts of the
+  // slices of the non-sink pages)
+  const bool slices = p.sel_mode == HX_SEL_SLICES;
+  const int nsl = slices ? p.list_stride - 1 : 1;
+  const int32_t* soff = slices ? p.lists + (int64_t)bh * p.list_stride : nullptr;
+  const int32_t soff_lo = (slices && tid < nsl) ? soff[tid] : 0, soff_hi = (slices && tid < nsl) ? soff[tid + 1] : 0;
+  const int32_t soff_all = slices ? soff[nsl] : 0;
 
   // dequant lanes: token t = lane >> 1, row half = lane & 1; x0 = which
   // 16-byte chunk of its half row (nuq4) the lane reads first is cx0
@@ -944,8 +948,10 @@ static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
     attr_set[dev] = true;
   }
   dim3 grid(p.n_splits, H, p.B);
-  decode_kernel<BK, BV><<<grid, NT, smem, s>>>(p);
-  HX_LAUNCH_CHECK();
+  if (hx_launch_pdl(decode_kernel<BK, BV>, grid, dim3(NT), smem, s, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return HX_ERR_LAUNCH;
+  }
   return HX_OK;
 }
 

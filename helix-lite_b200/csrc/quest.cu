@@ -328,6 +328,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   const int nb = (max_pages + kQPB - 1) / kQPB;  // batches per (b, h)
   const int64_t total = (int64_t)B * H * nb;
   const int64_t gw = (int64_t)blockIdx.x * kQW + warp, nw = (int64_t)gridDim.x * kQW;
+  pdl_allow_next();
   if (lane == 0) {
     for (int st = 0; st < kQStages; ++st) mbar_init(&sm.bar[warp][st], 1);
     fence_mbar_init();
@@ -335,6 +336,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   if (hist)
     for (int i = threadIdx.x; i < kQHistRows * kBins; i += blockDim.x) (&sm.hist[0][0])[i] = 0;
   __syncthreads();
+  pdl_wait();  // inputs (q, stats, tables, the histogram) may come from the kernels before
 
   // A warp takes a contiguous run of batches (so it rarely changes (b, h)):
   // batch k of this warp is global batch g0 + k. For a batch: its pages count
@@ -668,6 +670,8 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
   __shared__ uint64_t s_cand[kCandSmem];
   __shared__ uint32_t s_nc, s_above;
   __shared__ int s_last;
+  pdl_allow_next();
+  pdl_wait();  // the scores and the histogram come from the scoring kernel
   const int bh = blockIdx.y;
   const int b = bh / H;
   const int C = gridDim.x;
@@ -1078,10 +1082,12 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
     int64_t batches = (int64_t)B * H * ((max_pages + kQPB - 1) / kQPB);
     int64_t want = (batches + kQW - 1) / kQW;
     int grid = (int)(want < 148 ? want : 148);
-    quest_scores_tma_kernel<<<grid, kQW * 32, sizeof(QuestSmem), s>>>(
-        q, B, H, group, gqa_mode, (const uint16_t*)kmin, page_stride, head_stride, block_table, bt_stride,
-        seq_lens, page_size, max_pages, sink_pages, scores, hist, nullptr);
-    HX_LAUNCH_CHECK();
+    if (hx_launch_pdl(quest_scores_tma_kernel, dim3(grid), dim3(kQW * 32), sizeof(QuestSmem), s, q, B, H, group,
+                      gqa_mode, (const uint16_t*)kmin, page_stride, head_stride, block_table, bt_stride, seq_lens,
+                      page_size, max_pages, sink_pages, scores, hist, (uint32_t*)nullptr) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return HX_ERR_LAUNCH;
+    }
     return HX_OK;
   }
   if (stats_dtype == 1 && D == 128 && aligned) {
@@ -1137,10 +1143,12 @@ HX_API int hx_quest_threshold_slices(void* stream, const float* scores, int32_t 
     quest_hist_kernel<<<hg, 256, 0, st>>>(scores, H, seq_lens, page_size, max_pages, sink_pages, hist);
   }
   dim3 grid(quest_slices(max_pages), B * H);
-  quest_threshold_kernel<<<grid, 256, 0, st>>>(scores, H, seq_lens, page_size, max_pages, sink_pages,
-                                                       k_fixed, frac_num, frac_den, hist, cand, counters, thresh,
-                                                       slice_off, dev_err);
-  HX_LAUNCH_CHECK();
+  if (hx_launch_pdl(quest_threshold_kernel, grid, dim3(256), 0, st, scores, (int)H, seq_lens, (int)page_size,
+                    (int)max_pages, (int)sink_pages, (int)k_fixed, (int)frac_num, (int)frac_den, hist, cand, counters,
+                    thresh, slice_off, dev_err) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return HX_ERR_LAUNCH;
+  }
   return HX_OK;
 }
 
