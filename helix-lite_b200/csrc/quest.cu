@@ -756,6 +756,33 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
   if (!s_last) return;
   __threadfence();
 
+  // One round of loads feeds the whole finish: the candidate count, the
+  // candidates themselves (up to kCandSmem; reading past the count is harmless),
+  // the level-2 histogram and the slices' partial counts.
+  const bool gather = !trivial && bstar >= 0 && !full_bin;
+  const uint32_t ncap = (uint32_t)min(kCandSmem, max(max_pages, 1));
+  uint32_t cnt = 0;
+  int32_t part = 0;
+  if (slice_off && threadIdx.x < C && !trivial && bstar >= 0)
+    part = __ldcg(slice_off + (int64_t)bh * (C + 1) + threadIdx.x);
+  if (gather) {
+    cnt = *((volatile uint32_t*)&ctr[0]);
+    uint64_t kk[kCandSmem / 256];
+#pragma unroll
+    for (int u = 0; u < kCandSmem / 256; ++u) {
+      const uint32_t i = threadIdx.x + 256u * u;
+      kk[u] = i < ncap ? __ldcg(cand_bh + i) : 0ull;
+    }
+    if (!edge_bin(bstar)) load_hist(s_hist, hist2_bh);
+#pragma unroll
+    for (int u = 0; u < kCandSmem / 256; ++u) {
+      const uint32_t i = threadIdx.x + 256u * u;
+      if (i < ncap) s_cand[i] = kk[u];
+    }
+    __syncthreads();
+  }
+  const bool in_smem = cnt <= ncap;  // every candidate is in s_cand
+
   uint64_t T;
   if (pl.k_eff == 0) {
     T = ~0ull;
@@ -766,69 +793,63 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
     if (threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
   } else if (full_bin) {
     T = bin_floor(bstar, -1, anchor);
+  } else if (edge_bin(bstar)) {
+    T = in_smem ? radix_select<false>(s_cand, cnt, r, 0ull, 64, s_h2, s_warp, s_res)
+                : radix_select<true>(cand_bh, cnt, r, 0ull, 64, s_h2, s_warp, s_res);
   } else {
-    const uint32_t cnt = *((volatile uint32_t*)&ctr[0]);
-    if (edge_bin(bstar)) {
-      T = radix_select<true>(cand_bh, cnt, r, 0ull, 64, s_h2, s_warp, s_res);
+    uint32_t above2;
+    const int b2 = find_boundary(s_hist, r, above2, s_warp, s_res);
+    if (b2 < 0) {
+      T = bin_floor(bstar, -1, anchor);
+      if (threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
     } else {
-      load_hist(s_hist, hist2_bh);
-      __syncthreads();
-      uint32_t above2;
-      const int b2 = find_boundary(s_hist, r, above2, s_warp, s_res);
-      if (b2 < 0) {
-        T = bin_floor(bstar, -1, anchor);
-        if (threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
+      const uint32_t r2 = r - above2;
+      const uint32_t in_b2 = s_hist[b2];
+      if (in_b2 == r2) {
+        T = bin_floor(bstar, b2, anchor);
       } else {
-        const uint32_t r2 = r - above2;
-        if (s_hist[b2] == r2) {
-          T = bin_floor(bstar, b2, anchor);
+        // gather the level-2 boundary bin's keys (the histogram's smem is free
+        // now) and rank them
+        uint64_t* hand = reinterpret_cast<uint64_t*>(s_hist);
+        constexpr uint32_t kHand = kBins / 2;
+        __syncthreads();
+        if (threadIdx.x == 0) s_nc = 0;
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+          const uint64_t key = in_smem ? s_cand[i] : __ldcg(cand_bh + i);
+          if (bin2((uint32_t)(key >> 32), anchor) == b2) {
+            const uint32_t at = atomicAdd(&s_nc, 1u);
+            if (at < kHand) hand[at] = key;
+          }
+        }
+        __syncthreads();
+        const uint32_t nc = s_nc;
+        if (nc <= blockDim.x) {
+          // a handful of keys: key i is T when exactly r2 - 1 keys beat it
+          if (threadIdx.x == 0) s_res[0] = -1;
+          __syncthreads();
+          if (threadIdx.x < nc) {
+            const uint64_t mine = hand[threadIdx.x];
+            uint32_t beat = 0;
+            for (uint32_t i = 0; i < nc; ++i) beat += hand[i] > mine;
+            if (beat + 1 == r2) s_res[0] = (int)threadIdx.x;
+          }
+          __syncthreads();
+          const int w = s_res[0];
+          T = w >= 0 ? hand[w] : bin_floor(bstar, b2, anchor);
+          if (w < 0 && threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
+        } else if (nc <= kHand) {
+          T = radix_select<false>(hand, nc, r2, 0ull, 64, s_h2, s_warp, s_res);
         } else {
-          // gather the level-2 boundary bin's keys into smem and rank them
-          if (threadIdx.x == 0) s_nc = 0;
-          __syncthreads();
-          for (uint32_t i0 = 0; i0 < cnt; i0 += 16 * blockDim.x) {
-            uint64_t key[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              const uint32_t i = i0 + u * blockDim.x + threadIdx.x;
-              key[u] = i < cnt ? __ldcg(cand_bh + i) : 0ull;
-            }
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              if (i0 + u * blockDim.x + threadIdx.x < cnt && bin2((uint32_t)(key[u] >> 32), anchor) == b2) {
-                const uint32_t at = atomicAdd(&s_nc, 1u);
-                if (at < (uint32_t)kCandSmem) s_cand[at] = key[u];
-              }
-            }
-          }
-          __syncthreads();
-          const uint32_t nc = s_nc;
-          if (nc <= blockDim.x) {
-            // a handful of keys: key i is T when exactly r2 - 1 keys beat it
-            if (threadIdx.x == 0) s_res[0] = -1;
-            __syncthreads();
-            if (threadIdx.x < nc) {
-              const uint64_t mine = s_cand[threadIdx.x];
-              uint32_t beat = 0;
-              for (uint32_t i = 0; i < nc; ++i) beat += s_cand[i] > mine;
-              if (beat + 1 == r2) s_res[0] = (int)threadIdx.x;
-            }
-            __syncthreads();
-            const int w = s_res[0];
-            T = w >= 0 ? s_cand[w] : bin_floor(bstar, b2, anchor);
-            if (w < 0 && threadIdx.x == 0) set_err(err, HX_DEV_ERR_SELECT);
-          } else if (nc <= (uint32_t)kCandSmem) {
-            T = radix_select<false>(s_cand, nc, r2, 0ull, 64, s_h2, s_warp, s_res);
-          } else {
-            // more than kCandSmem keys within 16 units of key: rank the whole bin
-            T = radix_select<true>(cand_bh, cnt, r, 0ull, 64, s_h2, s_warp, s_res);
-          }
+          // more keys within 16 units of key than fit: rank the whole bin
+          T = in_smem ? radix_select<false>(s_cand, cnt, r, 0ull, 64, s_h2, s_warp, s_res)
+                      : radix_select<true>(cand_bh, cnt, r, 0ull, 64, s_h2, s_warp, s_res);
         }
       }
     }
   }
   if (slice_off) {
-    // final selected count of every slice, then the exclusive prefix
+    // final selected count of every slice, then the exclusive prefix (one warp)
     uint32_t* s_add = s_h2;  // C <= kMaxSlices <= 256 counters
     const int per = n_ns > 0 ? (n_ns + C - 1) / C : 1;
     __syncthreads();
@@ -837,14 +858,13 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
       if (pl.k_eff == 0) v = 0;
       else if (pl.k_eff >= n_ns) v = (uint32_t)max(0, min(per, n_ns - i * per));  // every page
       else if (bstar < 0) v = 0;
-      else v = (uint32_t)__ldcg(slice_off + (int64_t)bh * (C + 1) + i);
+      else v = (uint32_t)part;
       s_add[i] = v;
     }
     __syncthreads();
-    if (!trivial && bstar >= 0 && !full_bin) {
-      const uint32_t cnt = *((volatile uint32_t*)&ctr[0]);
+    if (gather) {
       for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-        const uint64_t key = __ldcg(cand_bh + i);
+        const uint64_t key = in_smem ? s_cand[i] : __ldcg(cand_bh + i);
         if (key >= T) {
           const int j = (int)(~(uint32_t)key);
           atomicAdd(&s_add[min((j - pl.sinks) / per, C - 1)], 1u);
@@ -852,14 +872,30 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
       }
       __syncthreads();
     }
-    if (threadIdx.x == 0) {
-      int32_t acc = 0;
-      for (int i = 0; i < C; ++i) {
-        const int32_t c = (int32_t)s_add[i];
-        slice_off[(int64_t)bh * (C + 1) + i] = acc;
-        acc += c;
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      uint32_t v[kMaxSlices / 32];
+      uint32_t sum = 0;
+#pragma unroll
+      for (int q = 0; q < kMaxSlices / 32; ++q) {
+        const int i = (kMaxSlices / 32) * lane + q;
+        v[q] = i < C ? s_add[i] : 0u;
+        sum += v[q];
       }
-      slice_off[(int64_t)bh * (C + 1) + C] = acc;
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += x;
+      }
+      uint32_t acc = incl - sum;
+#pragma unroll
+      for (int q = 0; q < kMaxSlices / 32; ++q) {
+        const int i = (kMaxSlices / 32) * lane + q;
+        if (i < C) slice_off[(int64_t)bh * (C + 1) + i] = (int32_t)acc;
+        acc += v[q];
+      }
+      if (lane == 31) slice_off[(int64_t)bh * (C + 1) + C] = (int32_t)incl;
     }
   }
   if (threadIdx.x == 0) {
