@@ -19,6 +19,8 @@
 // fp16 hi + lo parts so P.V keeps ~22 bits, V tile the same way, PV with two
 // MMAs per m-tile. Warps merge in smem; the last CTA of each (b, h) merges
 // the splits.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace hx {
@@ -44,6 +46,7 @@ struct DecodeParams {
   int bt_stride;
   const int32_t* seq_lens;
   int page_begin, max_pages, sel_mode;
+  int vphys;  // V positions from the physical page (HX_VPOS_PHYSICAL)
   const float* scores;
   const uint64_t* thresh;
   int sinks_req;
@@ -351,6 +354,15 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   auto v_bulk = [&](int pos0) -> bool {
     return pos0 + DS <= Tc && p.sc.levels_v == NLV && (reinterpret_cast<uintptr_t>(v_rows(pos0)) & 15u) == 0;
   };
+  // absolute position of slot 0 of list entry li, clamped to t_cal (every use
+  // only compares it with t_cal or reads rows below it): the logical page
+  // (page_begin + j) * 16, or with HX_VPOS_PHYSICAL the physical page
+  // (page_begin + block_table[j]) * 16, the reference pool's rule that a
+  // token's V row is its slot
+  auto vpos0 = [&](int li) -> int {
+    const int64_t pg = (int64_t)p.page_begin + (p.vphys ? sm.phys[li] : sm.pages[li]);
+    return (int)min(pg * DS, (int64_t)Tc);
+  };
   __syncthreads();
 
   for (int rb = ra; rb < re; rb += LISTCAP) {
@@ -478,7 +490,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
         const int pp = sm.phys[li];
         const uint4 dk = sm.dir[li][0], dv = sm.dir[li][1];
         const uint32_t ek = stage_k(dk.z), ev = stage_v(ek, dv.z);
-        const int pos0 = (p.page_begin + sm.pages[li]) * DS;
+        const int pos0 = vpos0(li);
         const bool vb = v_bulk(pos0);
         constexpr uint32_t VPB = 2u * DS * NLV;
         fence_proxy_async();
@@ -508,7 +520,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       const uint4 dk = sm.dir[li][0], dv = sm.dir[li][1];
       const uint32_t offk = dk.x, cntk = dk.z, offv = dv.x, cntv = dv.z;
       const int j = sm.pages[li];
-      const int pos0 = (p.page_begin + j) * DS;
+      const int pos0 = vpos0(li);
       const int valid = seq_len - j * DS;  // tokens of this page inside the sequence
 
       // ---- K tile: per-channel tables (lane = token t, half of the channels)
@@ -938,14 +950,16 @@ static inline cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s
 template <int BK, int BV>
 static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
   const size_t smem = sizeof(CtaSmem);
-  static bool attr_set[64] = {};
+  // per device, once: the attribute call is idempotent, so two threads that
+  // race here both set it and both store true
+  static std::atomic<bool> attr_set[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_ERR_LAUNCH;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(decode_kernel<BK, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
       return HX_ERR_LAUNCH;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   dim3 grid(p.n_splits, H, p.B);
   if (hx_launch_pdl(decode_kernel<BK, BV>, grid, dim3(NT), smem, s, p) != cudaSuccess) {
@@ -969,26 +983,36 @@ HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits) {
   return kCtrBytes + parts;
 }
 
-HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc, const uint16_t* q,
+// Validate a decode request and fill the kernel parameters (scratch aside).
+// Shared by hx_decode_attn and hx_decode_attn_noalloc so that both reject the
+// same requests before anything is queued on the stream.
+static int prepare_decode(DecodeParams& p, const hx_pool_layer* pool, const hx_layer_scales* sc, const uint16_t* q,
                           int32_t B, int32_t group, float softmax_scale, const int32_t* block_table,
                           int32_t bt_stride, const int32_t* seq_lens, int32_t page_begin, int32_t max_pages,
                           int32_t sel_mode, const float* scores, const uint64_t* thresh, int32_t sink_pages,
                           const int32_t* lists, int32_t list_stride, const int32_t* list_counts, int32_t n_splits,
-                          void* scratch, float* o, float* lse, uint16_t* out16, uint32_t* dev_err) {
-  if (!pool || !sc || !q || !seq_lens || !o || !lse || !scratch) return HX_ERR_ARG;
+                          float* o, float* lse, uint16_t* out16, uint32_t* dev_err) {
+  if (!pool || !sc || !q || !seq_lens || !o || !lse) return HX_ERR_ARG;
   if (B < 0 || group <= 0 || n_splits <= 0 || n_splits > MAXSPLIT || max_pages < 0 || page_begin < 0)
     return HX_ERR_ARG;
-  if (B == 0) return HX_OK;
+  if (pool->num_kv_heads <= 0 || pool->num_blocks <= 0 || !pool->codes || !pool->dir || !pool->arena)
+    return HX_ERR_ARG;
   if (pool->head_size != DD || pool->block_size != DS || group > 8) return HX_ERR_UNSUPPORTED;
   if ((pool->bits_k != 2 && pool->bits_k != 4) || (pool->bits_v != 2 && pool->bits_v != 4)) return HX_ERR_ARG;
-  if (sc->levels_k > (1 << pool->bits_k) || sc->levels_v > (1 << pool->bits_v) || sc->t_cal < 1) return HX_ERR_ARG;
+  if (!sc->k_poles || !sc->v_poles) return HX_ERR_ARG;
+  if (sc->levels_k < 1 || sc->levels_v < 1 || sc->levels_k > (1 << pool->bits_k) ||
+      sc->levels_v > (1 << pool->bits_v) || sc->t_cal < 1)
+    return HX_ERR_ARG;
+  if ((sel_mode & ~(HX_SEL_MODE_MASK | HX_VPOS_PHYSICAL)) != 0) return HX_ERR_ARG;
+  const int vphys = (sel_mode & HX_VPOS_PHYSICAL) ? 1 : 0;
+  sel_mode &= HX_SEL_MODE_MASK;
+  if (sel_mode < 0 || sel_mode > 3) return HX_ERR_ARG;
   if (sel_mode == HX_SEL_THRESHOLD && (!scores || !thresh)) return HX_ERR_ARG;
   if (sel_mode == HX_SEL_LIST && (!lists || !list_counts || list_stride <= 0)) return HX_ERR_ARG;
   if (sel_mode == HX_SEL_SLICES && (!scores || !thresh || !lists || list_stride < 2 || list_stride > NT + 1))
     return HX_ERR_ARG;
-  if (sel_mode < 0 || sel_mode > 3) return HX_ERR_ARG;
   if (block_table && bt_stride < max_pages) return HX_ERR_ARG;
-  DecodeParams p;
+  if ((int64_t)B * pool->num_kv_heads > kMaxBH) return HX_ERR_ARG;
   p.pool = *pool;
   p.sc = *sc;
   p.q = q;
@@ -1001,6 +1025,7 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
   p.page_begin = page_begin;
   p.max_pages = max_pages;
   p.sel_mode = sel_mode;
+  p.vphys = vphys;
   p.scores = scores;
   p.thresh = thresh;
   p.sinks_req = sink_pages;
@@ -1008,19 +1033,39 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
   p.list_stride = list_stride;
   p.list_counts = list_counts;
   p.n_splits = n_splits;
-  if ((int64_t)B * pool->num_kv_heads > kMaxBH) return HX_ERR_ARG;
-  p.ctr = reinterpret_cast<uint32_t*>(scratch);
-  p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCtrBytes);
   p.o = o;
   p.lse = lse;
   p.out16 = out16;
   p.err = dev_err;
-  cudaStream_t s = S_(stream);
-  const int H = pool->num_kv_heads;
-  if (pool->bits_k == 4 && pool->bits_v == 4) return launch_decode<4, 4>(p, H, s);
-  if (pool->bits_k == 4 && pool->bits_v == 2) return launch_decode<4, 2>(p, H, s);
-  if (pool->bits_k == 2 && pool->bits_v == 4) return launch_decode<2, 4>(p, H, s);
+  p.ctr = nullptr;
+  p.part = nullptr;
+  return HX_OK;
+}
+
+static int launch_prepared(DecodeParams& p, void* scratch, cudaStream_t s) {
+  p.ctr = reinterpret_cast<uint32_t*>(scratch);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCtrBytes);
+  const int H = p.pool.num_kv_heads;
+  if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4>(p, H, s);
+  if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2>(p, H, s);
+  if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4>(p, H, s);
   return launch_decode<2, 2>(p, H, s);
+}
+
+HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc, const uint16_t* q,
+                          int32_t B, int32_t group, float softmax_scale, const int32_t* block_table,
+                          int32_t bt_stride, const int32_t* seq_lens, int32_t page_begin, int32_t max_pages,
+                          int32_t sel_mode, const float* scores, const uint64_t* thresh, int32_t sink_pages,
+                          const int32_t* lists, int32_t list_stride, const int32_t* list_counts, int32_t n_splits,
+                          void* scratch, float* o, float* lse, uint16_t* out16, uint32_t* dev_err) {
+  DecodeParams p;
+  const int rc = prepare_decode(p, pool, sc, q, B, group, softmax_scale, block_table, bt_stride, seq_lens, page_begin,
+                                max_pages, sel_mode, scores, thresh, sink_pages, lists, list_stride, list_counts,
+                                n_splits, o, lse, out16, dev_err);
+  if (rc != HX_OK) return rc;
+  if (!scratch) return HX_ERR_ARG;
+  if (B == 0) return HX_OK;
+  return launch_prepared(p, scratch, S_(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -1035,22 +1080,23 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
 constexpr int64_t kStaticMaxSplitRows = 1024;  // B * H * n_splits at most
 constexpr int64_t kStaticScratchBytes = kCtrBytes + kStaticMaxSplitRows * PSZ * (int64_t)sizeof(float);
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
-static void* g_decode_scratch_addr[64];
+static std::atomic<void*> g_decode_scratch_addr[64];
 
 // The array's device address, looked up once per device with that device
-// current (host code may not use the symbol itself as a pointer).
+// current (host code may not use the symbol itself as a pointer). Threads
+// that race on the first call each look it up and store the same address.
 static int static_decode_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_ERR_LAUNCH;
-  if (!g_decode_scratch_addr[dev]) {
-    void* addr = nullptr;
+  void* addr = g_decode_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!addr) {
     if (cudaGetSymbolAddress(&addr, g_decode_scratch) != cudaSuccess || !addr) {
       (void)cudaGetLastError();
       return HX_ERR_LAUNCH;
     }
-    g_decode_scratch_addr[dev] = addr;
+    g_decode_scratch_addr[dev].store(addr, std::memory_order_release);
   }
-  *out = g_decode_scratch_addr[dev];
+  *out = addr;
   return HX_OK;
 }
 
@@ -1061,18 +1107,21 @@ HX_API int hx_decode_attn_noalloc(void* stream, const hx_pool_layer* pool, const
                                   const uint64_t* thresh, int32_t sink_pages, const int32_t* lists,
                                   int32_t list_stride, const int32_t* list_counts, int32_t n_splits, float* o,
                                   float* lse, uint16_t* out16, uint32_t* dev_err) {
-  if (!pool || B < 0 || n_splits <= 0) return HX_ERR_ARG;
+  // every argument is checked before anything is queued (the memset below)
+  DecodeParams p;
+  const int rc = prepare_decode(p, pool, sc, q, B, group, softmax_scale, block_table, bt_stride, seq_lens, page_begin,
+                                max_pages, sel_mode, scores, thresh, sink_pages, lists, list_stride, list_counts,
+                                n_splits, o, lse, out16, dev_err);
+  if (rc != HX_OK) return rc;
   if (B == 0) return HX_OK;
   if ((int64_t)B * pool->num_kv_heads * n_splits > kStaticMaxSplitRows) return HX_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
-  int rc = static_decode_scratch(&scratch);
-  if (rc != HX_OK) return rc;
+  const int rs = static_decode_scratch(&scratch);
+  if (rs != HX_OK) return rs;
   // the array keeps the previous call's contents: the split counters must start at zero
   if (cudaMemsetAsync(scratch, 0, (size_t)B * pool->num_kv_heads * sizeof(uint32_t), S_(stream)) != cudaSuccess)
     return HX_ERR_LAUNCH;
-  return hx_decode_attn(stream, pool, sc, q, B, group, softmax_scale, block_table, bt_stride, seq_lens, page_begin,
-                        max_pages, sel_mode, scores, thresh, sink_pages, lists, list_stride, list_counts, n_splits,
-                        scratch, o, lse, out16, dev_err);
+  return launch_prepared(p, scratch, S_(stream));
 }
 
 HX_API int hx_merge_partials(void* stream, const float* o_parts, const float* lse_parts, int32_t R, int32_t N,

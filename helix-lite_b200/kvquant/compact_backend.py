@@ -85,9 +85,9 @@ def make_impl_cls(base):
                 return
             slots = slot_mapping[:n].to(torch.int64)
             # a token's absolute position is taken as its slot, as the
-            # reference hook does (compact_backend.py:157-167): exact for one
-            # sequence per pool, and the V scales only distinguish positions
-            # below t_cal
+            # reference hook does (compact_backend.py:157-167); the decode
+            # reads V back with the same rule (v_pos="physical"), so a page's
+            # V scale rows follow its pool block wherever vLLM put it
             pool.write_kv(idx, key[:n].to(torch.float16), value[:n].to(torch.float16), slots, slots)
 
         def forward(self, layer, query, key, value, kv_cache, attn_metadata, output,
@@ -126,9 +126,9 @@ def decode_into(pool: CompactKVPool, idx: int, query: torch.Tensor, attn_metadat
     seq_lens = attn_metadata.seq_lens[:B]
     if _TOP_K > 0:
         sel = fused.quest_select(pool, idx, q, bt, seq_lens, top_k=_TOP_K, sink_pages=_SINK_BLOCKS, gqa=_GQA)
-        o, _ = fused.decode(pool, idx, q, bt, seq_lens, sel, softmax_scale=scale)
+        o, _ = fused.decode(pool, idx, q, bt, seq_lens, sel, softmax_scale=scale, v_pos="physical")
     else:
-        o, _ = fused.decode(pool, idx, q, bt, seq_lens, softmax_scale=scale)
+        o, _ = fused.decode(pool, idx, q, bt, seq_lens, softmax_scale=scale, v_pos="physical")
     out = output[:n].view(B, Hq, D)
     out.copy_(o.to(out.dtype))
     return output

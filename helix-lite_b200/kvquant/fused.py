@@ -149,7 +149,7 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
            seq_lens: torch.Tensor, selection: Selection | None = None, *, lists: torch.Tensor | None = None,
            list_counts: torch.Tensor | None = None, page_begin: int = 0, max_pages: int | None = None,
            n_splits: int | None = None, softmax_scale: float | None = None, out16: torch.Tensor | None = None,
-           o: torch.Tensor | None = None, lse: torch.Tensor | None = None):
+           o: torch.Tensor | None = None, lse: torch.Tensor | None = None, v_pos: str = "logical"):
     """Fused-dequant decode attention; returns (o (B, Hq, D) fp32, lse (B, Hq)).
 
     Pages attended: every page (no selection), the Quest selection (split
@@ -203,7 +203,8 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
         lstride = 0
     with torch.cuda.device(dev):
         call("hx_decode_attn", stream(dev), ctypes_ref(pool.layers[layer_idx].struct), ctypes_ref(st_scales),
-             ptr(q), B, Hq // H, scale, ptr(bt), bt.shape[1], ptr(sl), int(page_begin), mp, mode,
+             ptr(q), B, Hq // H, scale, ptr(bt), bt.shape[1], ptr(sl), int(page_begin), mp,
+             mode | (hxlib.VPOS_PHYSICAL if v_pos == "physical" else 0),
              ptr(selection.scores) if selection is not None else None,
              ptr(selection.thresh) if selection is not None else None,
              selection.sink_pages if selection is not None else 0,

@@ -241,6 +241,15 @@ HX_API int hx_quest_lists(void* stream, const float* scores, const uint64_t* thr
 #define HX_SEL_THRESHOLD 1   /* sinks + pages with key64 >= thresh          */
 #define HX_SEL_LIST      2   /* explicit per-(b, h) logical page lists      */
 #define HX_SEL_SLICES    3   /* sinks + key64 >= thresh, ranks located by slice_off */
+#define HX_SEL_MODE_MASK 0xFF
+/* OR-ed into sel_mode: the V scale row of page j's slot t is
+ * min((page_begin + block_table[j]) * 16 + t, t_cal - 1), i.e. the token's
+ * physical slot, the rule of the reference pool, which packs V with
+ * abs_positions = slot_mapping and unpacks block b from position b * 16
+ * (compact_backend.py:157-167, compact_pool.py:370-372, quest_selector.py:89).
+ * Without it the row is that of the logical position (page_begin + j) * 16 + t. */
+#define HX_VPOS_PHYSICAL 0x100
+
 
 /* Scratch bytes hx_decode_attn needs for B sequences, H heads, n_splits. */
 HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits);
@@ -249,7 +258,8 @@ HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits);
  * One decode token per sequence over the compact pool. q (B, H*group, D) fp16
  * (group <= 8, D = 128, page_size = 16). Logical page j of sequence b is pool
  * page block_table[b*bt_stride + j] and starts at absolute position
- * (page_begin + j) * 16 (V tail clamp); tokens >= seq_lens[b] are masked.
+ * (page_begin + j) * 16 (V tail clamp; (page_begin + block_table[...]) * 16
+ * with HX_VPOS_PHYSICAL in sel_mode); tokens >= seq_lens[b] are masked.
  * Selection: HX_SEL_DENSE; HX_SEL_THRESHOLD with scores / thresh from
  * hx_quest_scores / hx_quest_threshold; HX_SEL_LIST with lists (B, H,
  * list_stride) and list_counts (B, H); HX_SEL_SLICES with scores / thresh

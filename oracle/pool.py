@@ -169,18 +169,23 @@ class OraclePool:
                 sv[i, :, h] = v
         return sk, sv
 
-    def dequant_sequence(self, layer, block_table, n_tokens, page_offset=0):
+    def dequant_sequence(self, layer, block_table, n_tokens, page_offset=0, v_pos="logical"):
         """Dequantised (n_tokens, H, D) K and V of one sequence.
 
         Logical page j lives in pool page ``block_table[j]`` and starts at
-        absolute position ``(page_offset + j) * S``.
+        absolute position ``(page_offset + j) * S``; with v_pos="physical" its
+        V rows are those of ``(page_offset + block_table[j]) * S``, the
+        reference's rule (a slot is its position: compact_backend.py:157-167,
+        unpack from ``block_id * BS``: quest_selector.py:89,
+        compact_pool.py:370-372).
         """
         n_pages = -(-n_tokens // self.S)
         K = np.zeros((n_pages * self.S, self.H, self.D), np.float16)
         V = np.zeros_like(K)
         for j in range(n_pages):
             for h in range(self.H):
-                k, v = self.dequant_page(layer, h, int(block_table[j]), (page_offset + j) * self.S)
+                first = int(block_table[j]) if v_pos == "physical" else j
+                k, v = self.dequant_page(layer, h, int(block_table[j]), (page_offset + first) * self.S)
                 K[j * self.S:(j + 1) * self.S, h] = k
                 V[j * self.S:(j + 1) * self.S, h] = v
         return K[:n_tokens], V[:n_tokens]

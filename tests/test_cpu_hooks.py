@@ -87,6 +87,8 @@ def test_compact_decode_goes_to_the_fused_path(compact):
     assert calls[0][0] == "select" and calls[0][1] == 2 and calls[0][2] == (B, Hq, D)
     assert calls[0][3] == {"top_k": 8, "sink_pages": 4, "gqa": "mean"}
     assert calls[1][0] == "decode" and calls[1][2] == "sel" and calls[1][3]["softmax_scale"] == 0.125
+    # V is packed with abs_positions = slot, so it is read back by physical slot
+    assert calls[1][3]["v_pos"] == "physical"
     assert torch.all(out[:B] == 0.5) and torch.all(out[B:] == 0)
 
 

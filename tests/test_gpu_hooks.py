@@ -79,6 +79,70 @@ def test_compact_hook_decode_matches_oracle():
     assert (err <= TOL + np.abs(o) * 2.0 ** -11).all(), err.max()
 
 
+def test_compact_hook_shuffled_block_table_matches_oracle():
+    """vLLM hands out blocks from a free list (block 0 is its null block):
+    two sequences on shuffled, non-identity block tables, contexts longer
+    than t_cal. The hook packs V with abs_positions = slot (the reference
+    hook) and the decode must read each page's V rows at its physical slot
+    (reference: pack compact_pool.py:467 with compact_backend.py:157-167,
+    unpack quest_selector.py:89 + compact_pool.py:370-372)."""
+    from kvquant import compact_backend as cb
+    from kvquant.synthetic import NUQ4, make_kv, make_scales
+    H, D, S, G = 4, 128, 16, 7
+    lens = [3000, 1200]
+    t_cal, top_k = 256, 40
+    sc = make_scales([NUQ4], H, D, t_cal=t_cal, seed=90)
+    n_pages = [-(-n // S) for n in lens]
+    NB = sum(n_pages) + 37
+    backend = type("B", (FakeBackend,), {})
+    cb.install_compact_backend("", num_layers=1, num_blocks=NB, block_size=S, num_kv_heads=H, head_size=D,
+                               device="cuda", top_k_blocks_decode=top_k, sink_blocks=4, gqa="sum",
+                               scales=sc, backend_cls=backend, impl_cls=FakeImpl)
+    impl = backend.get_impl_cls()(scale=D ** -0.5)
+    layer = types.SimpleNamespace(layer_name="model.layers.0.self_attn.attn")
+    rng = np.random.default_rng(91)
+    free = rng.permutation(np.arange(1, NB))              # block 0 is never handed out
+    bt = np.zeros((2, max(n_pages)), np.int32)
+    bt[0, :n_pages[0]] = free[:n_pages[0]]
+    bt[1, :n_pages[1]] = free[n_pages[0]:n_pages[0] + n_pages[1]]
+    assert not np.array_equal(bt[0, :n_pages[0]], np.arange(n_pages[0]))
+    orc = OraclePool(1, NB, S, H, D, oracle_scales(sc))
+    for b, n in enumerate(lens):
+        K, V = make_kv(n, H, D, seed=92 + b, chan_seed=90)
+        pos = np.arange(n)
+        slots = torch.from_numpy(bt[b, pos // S].astype(np.int64) * S + pos % S).cuda()
+        for a in range(0, n, 700):                        # chunked prefill, one cache update per chunk
+            impl.do_kv_cache_update(layer, K[a:a + 700], V[a:a + 700], None, slots[a:a + 700])
+        orc.write_kv(0, np16(K), np16(V), np16(slots), np16(slots))
+    cb.pool().check()
+    g = torch.Generator(device="cuda").manual_seed(93)
+    q = torch.randn((2, H * G, D), generator=g, device="cuda").to(torch.float16)
+    meta = types.SimpleNamespace(max_query_len=1, num_actual_tokens=2, causal=True,
+                                 block_table=torch.from_numpy(bt).cuda(),
+                                 seq_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"))
+    out = torch.zeros((2, H * G, D), dtype=torch.float16, device="cuda")
+    impl.forward(layer, q, q[:, :H], q[:, :H], None, meta, out)
+    cb.pool().check()
+    assert not impl.sent
+    for b, n in enumerate(lens):
+        used = bt[b, :n_pages[b]]
+        kmin = orc.stats[0][:, used, 0].transpose(1, 0, 2)
+        kmax = orc.stats[0][:, used, 1].transpose(1, 0, 2)
+        qp, qn = oq.group_terms(np16(q[b]), G, "sum")
+        ref = oq.page_scores(qp, qn, kmin, kmax)
+        pages = [oq.select_pages(ref[:, h], top_k, 4) for h in range(H)]
+        mask = oatt.page_mask_to_token_mask(pages, n, S)
+        qd = np16(q[b]).astype(np.float64)
+        Kd, Vd = orc.dequant_sequence(0, used, n, v_pos="physical")
+        o, _ = oatt.decode_attention(qd, Kd, Vd, mask)
+        # the case discriminates: the logical-position rule gives another answer
+        _, Vl = orc.dequant_sequence(0, used, n, v_pos="logical")
+        o_logical, _ = oatt.decode_attention(qd, Kd, Vl, mask)
+        assert np.abs(o_logical - o).max() > 10 * TOL
+        err = np.abs(np16(out[b]).astype(np.float64) - o)
+        assert (err <= TOL + np.abs(o) * 2.0 ** -11).all(), (b, err.max())
+
+
 def test_quantise_dequantise_hook_matches_oracle():
     from kvquant import vllm_backend as vb
     from kvquant.synthetic import NUQ4, make_kv, make_scales
