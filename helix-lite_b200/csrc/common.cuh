@@ -155,6 +155,12 @@ static inline cudaError_t hx_launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// Bandwidth path of hx_pack_append (pack_fast.cu): HX_ERR_UNSUPPORTED when
+// the request does not fit it (page size, head size, missing thresholds).
+int hx_pack_fast_launch(cudaStream_t s, const hx_pool_layer* pool, const hx_layer_scales* sc, const uint16_t* key,
+                        const uint16_t* value, const int64_t* slots, const int64_t* abspos, int32_t T,
+                        uint32_t* dev_err);
+
 // Host-side launch check shared by the C entry points.
 #define HX_LAUNCH_CHECK()                                   \
   do {                                                      \

@@ -844,19 +844,21 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
 // ---------------------------------------------------------------------------
 // cross-shard merge of normalised (o, lse)
 
-__global__ void merge_kernel(const float* o_parts, const float* lse_parts, int R, int N, int D, float* o, float* lse,
-                             uint16_t* out16) {
+// Rank r's partials: o at o_parts + r * o_stride (N x D), lse at
+// lse_parts + r * lse_stride (N).
+__global__ void merge_kernel(const float* o_parts, const float* lse_parts, int64_t o_stride, int64_t lse_stride, int R,
+                             int N, int D, float* o, float* lse, uint16_t* out16) {
   const int i = blockIdx.x;
   float M = -INFINITY;
-  for (int r = 0; r < R; ++r) M = fmaxf(M, lse_parts[(int64_t)r * N + i]);
+  for (int r = 0; r < R; ++r) M = fmaxf(M, lse_parts[(int64_t)r * lse_stride + i]);
   const float base = M == -INFINITY ? 0.0f : M;
   float W = 0.0f;
-  for (int r = 0; r < R; ++r) W += expf(lse_parts[(int64_t)r * N + i] - base);
+  for (int r = 0; r < R; ++r) W += expf(lse_parts[(int64_t)r * lse_stride + i] - base);
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.0f;
     for (int r = 0; r < R; ++r) {
-      float w = expf(lse_parts[(int64_t)r * N + i] - base);
-      if (w > 0.0f) acc += w * o_parts[((int64_t)r * N + i) * D + d];
+      float w = expf(lse_parts[(int64_t)r * lse_stride + i] - base);
+      if (w > 0.0f) acc += w * o_parts[(int64_t)r * o_stride + (int64_t)i * D + d];
     }
     float v = W > 0.0f ? acc / W : 0.0f;
     o[(int64_t)i * D + d] = v;
@@ -1129,7 +1131,18 @@ HX_API int hx_merge_partials(void* stream, const float* o_parts, const float* ls
   if (R <= 0 || N < 0 || D <= 0) return HX_ERR_ARG;
   if (N == 0) return HX_OK;
   if (!o_parts || !lse_parts || !o || !lse) return HX_ERR_ARG;
-  merge_kernel<<<N, 128, 0, S_(stream)>>>(o_parts, lse_parts, R, N, D, o, lse, out16);
+  merge_kernel<<<N, 128, 0, S_(stream)>>>(o_parts, lse_parts, (int64_t)N * D, (int64_t)N, R, N, D, o, lse, out16);
+  HX_LAUNCH_CHECK();
+  return HX_OK;
+}
+
+HX_API int hx_merge_gathered(void* stream, const float* gathered, int32_t R, int32_t N, int32_t D, float* o,
+                             float* lse, uint16_t* out16) {
+  if (R <= 0 || N < 0 || D <= 0) return HX_ERR_ARG;
+  if (N == 0) return HX_OK;
+  if (!gathered || !o || !lse) return HX_ERR_ARG;
+  const int64_t row = (int64_t)N * (D + 1);
+  merge_kernel<<<N, 128, 0, S_(stream)>>>(gathered, gathered + (int64_t)N * D, row, row, R, N, D, o, lse, out16);
   HX_LAUNCH_CHECK();
   return HX_OK;
 }

@@ -89,7 +89,7 @@ HX_DEVINL uint32_t filter_slots(uint32_t* arena, uint32_t off, uint32_t cnt, int
     uint32_t e = 0;
     bool keep = false;
     if (i < cnt) {
-      e = arena[off + i];
+      e = __ldcg(arena + off + i);
       int t = (e >> 24) & 31;
       keep = (t < t0) || (t >= t1);
     }
@@ -118,7 +118,7 @@ HX_DEVINL bool ensure_capacity(const hx_pool_layer& pool, OutList& L, uint32_t n
     ok = __shfl_sync(0xffffffffu, ok, 0);
     new_off = __shfl_sync(0xffffffffu, new_off, 0);
     if (!ok) return false;
-    for (uint32_t i = lane; i < L.cnt; i += 32) pool.arena[new_off + i] = pool.arena[L.off + i];
+    for (uint32_t i = lane; i < L.cnt; i += 32) pool.arena[new_off + i] = __ldcg(pool.arena + L.off + i);
     __syncwarp();
     L.off = new_off;
     L.cap = new_cap;
@@ -151,7 +151,7 @@ HX_DEVINL void append_row(const hx_pool_layer& pool, OutList& L, const uint32_t 
 }
 
 HX_DEVINL void atomic_min_f16(uint16_t* addr, uint16_t v, uint32_t* err) {
-  uint16_t old = *addr;
+  uint16_t old = __ldcg(addr);
   for (int it = 0; it < 256; ++it) {
     if (!(h2f(v) < h2f(old))) return;
     uint16_t prev = atomicCAS(reinterpret_cast<unsigned short*>(addr), old, v);
@@ -162,7 +162,7 @@ HX_DEVINL void atomic_min_f16(uint16_t* addr, uint16_t v, uint32_t* err) {
 }
 
 HX_DEVINL void atomic_max_f16(uint16_t* addr, uint16_t v, uint32_t* err) {
-  uint16_t old = *addr;
+  uint16_t old = __ldcg(addr);
   for (int it = 0; it < 256; ++it) {
     if (!(h2f(v) > h2f(old))) return;
     uint16_t prev = atomicCAS(reinterpret_cast<unsigned short*>(addr), old, v);
@@ -185,9 +185,27 @@ HX_DEVINL void store_row(uint8_t* dst, const uint8_t* codes, int D, int bits) {
 
 // One warp per (run leader token, head). A run is a maximal stretch of input
 // tokens that fill consecutive slots of one page; the leader processes it in
-// slot order, so page lists and stats of a page have a single writer per
-// launch (tokens of a page must be contiguous in the input, as vLLM's
-// slot_mapping is).
+// slot order. A page whose slots come as several runs in one launch (tokens in
+// any order) is updated one run at a time: the warp holds the page lock (bit
+// 31 of the K directory record's rows word) while it edits the page's lists.
+constexpr uint32_t kGenericPageLock = 0x80000000u;
+
+// Take / release a page lock (whole warp; bounded spin, false = gave up).
+HX_DEVINL bool generic_page_lock(uint32_t* rows_word, uint32_t* err) {
+  uint32_t got = 0;
+  if (lane_id() == 0) {
+    for (uint32_t it = 0; it < (1u << 20); ++it) {
+      if ((atomicOr(rows_word, kGenericPageLock) & kGenericPageLock) == 0u) {
+        got = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (!got) set_err(err, HX_DEV_ERR_TIMEOUT);
+    __threadfence();
+  }
+  return __shfl_sync(0xffffffffu, got, 0) != 0;
+}
 template <int KD, int LK, int LV>
 __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx_layer_scales sc,
                                                           const uint16_t* __restrict__ key,
@@ -244,14 +262,19 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
     rmax[k] = __int_as_float(0xff800000);
   }
 
+  if (!generic_page_lock(dir_ptr(pool, h, pg, 0) + 3, err)) return;
   OutList LKs, LVs;
   {
     uint32_t* dk = dir_ptr(pool, h, pg, 0);
     uint32_t* dv = dir_ptr(pool, h, pg, 1);
-    LKs = {dk[0], dk[1], dk[2], dk[3]};
-    LVs = {dv[0], dv[1], dv[2], dv[3]};
-    if ((int)LKs.rows > t0) LKs.cnt = filter_slots(pool.arena, LKs.off, LKs.cnt, t0, t0 + n);
-    if ((int)LVs.rows > t0) LVs.cnt = filter_slots(pool.arena, LVs.off, LVs.cnt, t0, t0 + n);
+    // rows (slots written) live in the K record; the V record's last word is
+    // the bandwidth kernel's per-launch run count, zero between launches
+    LKs = {__ldcg(dk), __ldcg(dk + 1), __ldcg(dk + 2), __ldcg(dk + 3) & ~kGenericPageLock};
+    LVs = {__ldcg(dv), __ldcg(dv + 1), __ldcg(dv + 2), 0u};
+    if ((int)LKs.rows > t0) {
+      LKs.cnt = filter_slots(pool.arena, LKs.off, LKs.cnt, t0, t0 + n);
+      LVs.cnt = filter_slots(pool.arena, LVs.off, LVs.cnt, t0, t0 + n);
+    }
   }
 
   // Count the run's outliers first and size the page lists once, so a
@@ -345,12 +368,16 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
       atomic_max_f16(st + D + d, f2h(rmax[k]), err);
     }
   }
+  __threadfence();  // entries and stats visible before the page is released
+  __syncwarp();
   if (lane == 0) {
     uint32_t rows_new = (uint32_t)(t0 + n);
     uint32_t* dk = dir_ptr(pool, h, pg, 0);
     uint32_t* dv = dir_ptr(pool, h, pg, 1);
-    dk[0] = LKs.off; dk[1] = LKs.cap; dk[2] = LKs.cnt; dk[3] = max(LKs.rows, rows_new);
-    dv[0] = LVs.off; dv[1] = LVs.cap; dv[2] = LVs.cnt; dv[3] = max(LVs.rows, rows_new);
+    dk[0] = LKs.off; dk[1] = LKs.cap; dk[2] = LKs.cnt;
+    dv[0] = LVs.off; dv[1] = LVs.cap; dv[2] = LVs.cnt;
+    __threadfence();
+    atomicExch(dk + 3, max(LKs.rows, rows_new));  // rows, lock bit clear
   }
 }
 
@@ -654,6 +681,10 @@ HX_API int hx_pack_append(void* stream, const hx_pool_layer* pool, const hx_laye
   if (!key || !value || !slot_mapping || !abs_positions) return HX_ERR_ARG;
   const int D = pool->head_size;
   if (D > 128) return HX_ERR_UNSUPPORTED;
+  {
+    const int rc = hx_pack_fast_launch(S_(stream), pool, sc, key, value, slot_mapping, abs_positions, T, dev_err);
+    if (rc != HX_ERR_UNSUPPORTED) return rc;
+  }
   int64_t warps = (int64_t)T * pool->num_kv_heads;
   int64_t blocks = (warps + 3) / 4;
   if (blocks > 0x7fffffff) return HX_ERR_ARG;

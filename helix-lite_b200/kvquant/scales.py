@@ -13,6 +13,7 @@ so existing ``.pt`` scale files load unchanged:
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass, field
 
 import torch
@@ -94,7 +95,10 @@ class KVScales:
 
         Poles and thresholds become contiguous fp16 on the device once and are
         cached; the reference kernels read fp16 scales too
-        (src/kvquant/compact_pool.py:222-287).
+        (src/kvquant/compact_pool.py:222-287). The code thresholds the pack
+        kernel bisects (hx_scales_prepare: per codebook row, the fp16 values
+        where the reference's nearest-pole scan moves to the next level) are
+        computed on the device with them, once per layer and device.
         """
         dev = torch.device(device)
         key = (layer, dev.type, dev.index)
@@ -107,8 +111,17 @@ class KVScales:
             return t.to(device=dev, dtype=torch.float16).contiguous()
         ts = [f16(ks.poles), f16(ks.upper_threshold), f16(ks.lower_threshold),
               f16(vs.poles), f16(vs.upper_threshold), f16(vs.lower_threshold)]
-        st = LayerScales(*(t.data_ptr() for t in ts), int(ks.poles.shape[-1]), int(vs.poles.shape[-1]),
-                         int(vs.poles.shape[1]), 0)
+        H, D, levels_k = (int(x) for x in ks.poles.shape)
+        t_cal, levels_v = int(vs.poles.shape[1]), int(vs.poles.shape[-1])
+        st = LayerScales(*(t.data_ptr() for t in ts), levels_k, levels_v, t_cal, 0, None, None)
+        if D % 2 == 0 and levels_k <= 16 and levels_v <= 16:
+            from hxlib import call, ptr, stream
+            kt = torch.empty((H, D // 2, 16), dtype=torch.int32, device=dev)
+            vt = torch.empty((H, t_cal, 16), dtype=torch.int32, device=dev)
+            with torch.cuda.device(dev):
+                call("hx_scales_prepare", stream(dev), ctypes.byref(st), H, D, ptr(kt), ptr(vt))
+            st.k_thresh, st.v_thresh = kt.data_ptr(), vt.data_ptr()
+            ts += [kt, vt]
         hit = (st, ts)
         self._dev_cache[key] = hit
         return hit

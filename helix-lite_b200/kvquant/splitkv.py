@@ -40,18 +40,67 @@ def local_k(shard: Shard, frac=(1, 4)) -> int:
     return shard.n_pages * frac[0] // frac[1]
 
 
+class Exchange:
+    """Preallocated exchange of one layer's split-KV partials.
+
+    Each rank's row is [o (N x D) | lse (N)] fp32 in ``send``; one
+    ``all_gather_into_tensor`` fills ``recv`` (R rows) and the merge kernel
+    reads it in place (hx_merge_gathered), so a layer costs one collective and
+    one small kernel, with no allocation or concatenation (the step can be
+    captured in a CUDA graph). The decode may write straight into ``o_view`` /
+    ``lse_view``.
+    """
+
+    def __init__(self, N: int, D: int, world: int, device, group=None):
+        self.N, self.D, self.world, self.group = N, D, world, group
+        self.send = torch.empty((N * (D + 1),), dtype=torch.float32, device=device)
+        self.recv = torch.empty((world, N * (D + 1)), dtype=torch.float32, device=device)
+        self.lse_out = torch.empty((N,), dtype=torch.float32, device=device)
+        self.o_view = self.send[:N * D].view(N, D)
+        self.lse_view = self.send[N * D:]
+
+    def gather(self, o: torch.Tensor, lse: torch.Tensor):
+        """All-gather; returns (R, N, D) and (R, N) views of the received rows."""
+        if o.data_ptr() != self.o_view.data_ptr():
+            self.o_view.copy_(o.reshape(self.N, self.D))
+        if lse.data_ptr() != self.lse_view.data_ptr():
+            self.lse_view.copy_(lse.reshape(self.N))
+        dist.all_gather_into_tensor(self.recv.view(-1), self.send, group=self.group)
+        nd = self.N * self.D
+        return self.recv[:, :nd].view(self.world, self.N, self.D), self.recv[:, nd:]
+
+    def merge(self, o: torch.Tensor, lse: torch.Tensor, out: torch.Tensor, out16: torch.Tensor | None = None):
+        """Exchange and merge into ``out`` (N, D) fp32; returns (out, lse)."""
+        import hxlib
+        self.gather(o, lse)
+        dev = self.send.device
+        with torch.cuda.device(dev):
+            hxlib.call("hx_merge_gathered", hxlib.stream(dev), hxlib.ptr(self.recv), self.world, self.N, self.D,
+                       hxlib.ptr(out), hxlib.ptr(self.lse_out), hxlib.ptr(out16))
+        return out, self.lse_out
+
+
+_EXCHANGES: dict = {}
+
+
+def _exchange(N: int, D: int, device, group=None) -> Exchange:
+    world = dist.get_world_size(group)
+    key = (N, D, str(device), world, id(group))
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = _EXCHANGES[key] = Exchange(N, D, world, device, group)
+    return ex
+
+
 def exchange_partials(o: torch.Tensor, lse: torch.Tensor, group=None):
     """All-gather normalised partials: o (N, D), lse (N,) -> (R, N, D), (R, N).
 
-    o and lse travel in one buffer so the exchange is a single collective.
+    o and lse travel in one buffer (cached per shape and device) so the
+    exchange is a single collective; the results are views of that buffer,
+    valid until the next exchange of the same shape.
     """
     N, D = o.shape
-    world = dist.get_world_size(group)
-    send = torch.cat([o.reshape(-1).float(), lse.reshape(-1).float()])
-    recv = torch.empty((world * send.numel(),), dtype=send.dtype, device=send.device)
-    dist.all_gather_into_tensor(recv, send, group=group)
-    recv = recv.view(world, send.numel())
-    return recv[:, :N * D].reshape(world, N, D), recv[:, N * D:].reshape(world, N)
+    return _exchange(N, D, o.device, group).gather(o.float(), lse.float())
 
 
 def splitkv_decode(pool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
@@ -63,14 +112,15 @@ def splitkv_decode(pool, layer_idx: int, query: torch.Tensor, block_table: torch
     tokens; ``shard.page_begin`` places them in the global sequence (V's
     position clamp). Returns the merged (o (B, Hq, D) fp32, lse (B, Hq)).
     """
-    from .fused import decode, merge_partials, quest_select
+    from .fused import decode, quest_select
     B, Hq, D = query.shape
     sel = None
     if quest:
         sel = quest_select(pool, layer_idx, query, block_table, seq_lens, top_k=local_k(shard, frac),
                            sink_pages=shard.sink_pages, gqa=gqa)
-    o, lse = decode(pool, layer_idx, query, block_table, seq_lens, sel, page_begin=shard.page_begin,
-                    n_splits=n_splits)
-    O, L = exchange_partials(o.view(B * Hq, D), lse.view(B * Hq), group)
-    om, lm = merge_partials(O, L, out16)
-    return om.view(B, Hq, D), lm.view(B, Hq)
+    ex = _exchange(B * Hq, D, query.device, group)
+    decode(pool, layer_idx, query, block_table, seq_lens, sel, page_begin=shard.page_begin, n_splits=n_splits,
+           o=ex.o_view.view(B, Hq, D), lse=ex.lse_view.view(B, Hq))
+    om = torch.empty((B * Hq, D), dtype=torch.float32, device=query.device)
+    om, lm = ex.merge(ex.o_view, ex.lse_view, om, out16)
+    return om.view(B, Hq, D), lm.clone().view(B, Hq)

@@ -62,6 +62,10 @@ typedef struct hx_layer_scales {
   int32_t levels_v;          /* 2..16 */
   int32_t t_cal;             /* V positions >= t_cal use row t_cal - 1     */
   int32_t reserved;
+  /* Code thresholds written by hx_scales_prepare (device, 16-byte aligned),
+   * or NULL: hx_pack_append then takes its level-scan kernel.            */
+  const uint32_t* k_thresh;  /* (H, D/2, 16) fp16 pairs                   */
+  const uint32_t* v_thresh;  /* (H, t_cal, 16) fp16 duplicated in both halves */
 } hx_layer_scales;
 
 /*
@@ -105,11 +109,35 @@ HX_API int hx_pool_reset_pages(void* stream, const hx_pool_layer* pool,
  * token at position min(abs_positions[t], t_cal - 1); outliers (outside the
  * band) appended to the page lists; K page stats updated with the running
  * min / max of the reconstructed K. slot_mapping[t] < 0 skips the token.
- * Replaces CompactKVPool.write_kv (compact_pool.py:447-489). */
+ * Tokens may come in any slot order: a page whose slots arrive as several
+ * runs in one call (a run = input tokens filling consecutive slots) is
+ * updated one run at a time under a per-page lock, so no outlier entry or
+ * stat is lost. A slot written twice in one call keeps one of its tokens,
+ * unspecified which (the reference's parallel kernels race the same way).
+ * The order of entries inside a page's outlier list is unspecified.
+ * With 16-token pages, head_size 128 and the scales' thresholds
+ * (hx_scales_prepare) a bandwidth kernel runs; otherwise a level-scan kernel.
+ * Both give the same bytes. Replaces CompactKVPool.write_kv
+ * (compact_pool.py:447-489). */
 HX_API int hx_pack_append(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
                           const uint16_t* key, const uint16_t* value,      /* (T, H, D) fp16 */
                           const int64_t* slot_mapping, const int64_t* abs_positions,
                           int32_t T, uint32_t* dev_err);
+
+/* Code thresholds of a layer's codebooks for the bandwidth path of
+ * hx_pack_append (16-token pages, head_size 128). For a codebook row with
+ * poles p_0 < ... < p_{L-1} (finite), entry l < L-1 is the largest fp16 x for
+ * which the reference's scan does not prefer level l+1 over level l
+ * (|x - p_{l+1}| < |x - p_l| in fp32, compact_pool.py:258-268), entries up to
+ * 14 are +inf, and entry 15 is a bound X below which the count of thresholds
+ * under x is the scan's code (X = p_0 + 2^22 * smallest gap, rounded down).
+ * Rows whose poles are not finite and strictly increasing get X = -inf; the
+ * pack kernel runs the scan itself for every element with !(x < X). Layout:
+ * k_thresh (H, D/2, 16) u32, half e of entry l of pair P from channel 2P+e;
+ * v_thresh (H, t_cal, 16) u32, each entry's fp16 in both halves. Computed once
+ * per scales (no reference counterpart: the reference scans every level). */
+HX_API int hx_scales_prepare(void* stream, const hx_layer_scales* sc, int32_t H, int32_t D,
+                             uint32_t* k_thresh, uint32_t* v_thresh);
 
 /* Dequantise whole pages to fp16 staging (NK, S, H, D) for K and V.
  * Replaces CompactKVPool.unpack_to_staging (compact_pool.py:492-537). */
@@ -250,7 +278,6 @@ HX_API int hx_quest_lists(void* stream, const float* scores, const uint64_t* thr
  * Without it the row is that of the logical position (page_begin + j) * 16 + t. */
 #define HX_VPOS_PHYSICAL 0x100
 
-
 /* Scratch bytes hx_decode_attn needs for B sequences, H heads, n_splits. */
 HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits);
 
@@ -314,6 +341,12 @@ HX_API int hx_decode_attn_noalloc(void* stream, const hx_pool_layer* pool, const
  * all-gather of split-KV partials across GPUs. */
 HX_API int hx_merge_partials(void* stream, const float* o_parts, const float* lse_parts,
                              int32_t R, int32_t N, int32_t D, float* o, float* lse, uint16_t* out16);
+
+/* The same merge over the buffer an all-gather of per-rank rows
+ * [o (N x D) | lse (N)] fills: gathered (R, N * (D + 1)) fp32, read in place
+ * (the exchange of the split-KV step sends one such row per rank). */
+HX_API int hx_merge_gathered(void* stream, const float* gathered, int32_t R, int32_t N, int32_t D, float* o,
+                             float* lse, uint16_t* out16);
 
 /*
  * selected_attention on dense pages (quest/reference.py:136-168), fp32

@@ -60,11 +60,19 @@ def code_bits(levels: int) -> int:
 
 
 def quantize_k_rows(x, sc: LayerScalesNP):
-    """K rows x (N, H, D) fp16 -> codes (N, H, D), mask, recon fp16."""
+    """K rows x (N, H, D) fp16 -> codes (N, H, D), mask, recon fp16.
+
+    The reconstruction of a non-outlier is its pole; when no level is closer
+    than +inf (x NaN or infinite) the reference's scan keeps its initial pole
+    0.0 (compact_pool.py:260-268), and so does this.
+    """
     codes = nearest_codes(x, sc.k_poles[None])
     mask = band_outliers(x, sc.k_upper[None], sc.k_lower[None])
     pole = np.take_along_axis(np.broadcast_to(sc.k_poles[None], x.shape + (sc.k_poles.shape[-1],)),
                               codes[..., None].astype(np.int64), axis=-1)[..., 0]
+    d = np.abs(x.astype(np.float32)[..., None] - sc.k_poles[None].astype(np.float32))
+    none_closer = ~(d < np.float32(np.inf)).any(axis=-1)
+    pole = np.where(none_closer, np.float16(0.0), pole)
     recon = np.where(mask, x, pole).astype(np.float16)
     return codes, mask, recon
 
@@ -81,11 +89,21 @@ def quantize_v_rows(x, pos, sc: LayerScalesNP):
 
 
 class OraclePool:
+    """The pool's contents, written and read the reference's way.
+
+    Outliers are kept densely per slot (``outm`` / ``outv``: (H, NB, S, D) per
+    layer and K|V, allocated on first write), which is the reference's own
+    storage (compact_pool.py:426-432); ``outlier_entries`` / ``outlier_array``
+    list them in the build's sparse form for comparison.
+    """
+
     def __init__(self, num_layers, num_blocks, block_size, num_kv_heads, head_size, scales):
         self.L, self.NB, self.S = num_layers, num_blocks, block_size
         self.H, self.D = num_kv_heads, head_size
         self.scales = list(scales)
-        self.codes, self.stats, self.rows = [], [], []
+        self.codes, self.stats = [], []
+        self.outm = [[None, None] for _ in self.scales]
+        self.outv = [[None, None] for _ in self.scales]
         for sc in self.scales:
             self.codes.append((np.zeros((self.H, self.NB, self.S, self.D * sc.bits_k // 8), np.uint8),
                                np.zeros((self.H, self.NB, self.S, self.D * sc.bits_v // 8), np.uint8)))
@@ -93,11 +111,18 @@ class OraclePool:
             st[:, :, 0] = np.float16(np.inf)
             st[:, :, 1] = np.float16(-np.inf)
             self.stats.append(st)
-            # rows[(h, page, kv, slot)] = (d_idx uint8 array, values fp16 array)
-            self.rows.append({})
+
+    def _outliers(self, layer, kv):
+        if self.outm[layer][kv] is None:
+            shape = (self.H, self.NB, self.S, self.D)
+            self.outm[layer][kv] = np.zeros(shape, bool)
+            self.outv[layer][kv] = np.zeros(shape, np.float16)
+        return self.outm[layer][kv], self.outv[layer][kv]
 
     # -- write side (compact_pool.py:447-489) --
     def write_kv(self, layer, key, value, slot_mapping, abs_positions):
+        """Tokens are written in input order: a slot written twice keeps the
+        later token, and its outlier row is replaced, as the dense store does."""
         sc = self.scales[layer]
         key = np.asarray(key, np.float16)
         value = np.asarray(value, np.float16)
@@ -112,64 +137,73 @@ class OraclePool:
         kp = pack_codes(kc, sc.bits_k)
         vp = pack_codes(vc, sc.bits_v)
         pages, t = slots // self.S, slots % self.S
-        codes, stats, rows = self.codes[layer], self.stats[layer], self.rows[layer]
-        for i in range(slots.shape[0]):
-            pg, s = pages[i], t[i]
-            for h in range(self.H):
-                codes[0][h, pg, s] = kp[i, h]
-                codes[1][h, pg, s] = vp[i, h]
-                stats[h, pg, 0] = np.minimum(stats[h, pg, 0], krec[i, h])
-                stats[h, pg, 1] = np.maximum(stats[h, pg, 1], krec[i, h])
-                for kv, (m, x) in enumerate(((km, key), (vm, value))):
-                    d = np.nonzero(m[i, h])[0].astype(np.uint8)
-                    rows[(h, int(pg), kv, int(s))] = (d, x[i, h, d].astype(np.float16))
+        codes, stats = self.codes[layer], self.stats[layer]
+        # numpy assigns repeated indices in order, so the last token of a slot wins
+        codes[0][:, pages, t] = kp.transpose(1, 0, 2)
+        codes[1][:, pages, t] = vp.transpose(1, 0, 2)
+        for h in range(self.H):
+            np.minimum.at(stats[h, :, 0], pages, krec[:, h])
+            np.maximum.at(stats[h, :, 1], pages, krec[:, h])
+        for kv, (m, x) in enumerate(((km, key), (vm, value))):
+            om, ov = self._outliers(layer, kv)
+            om[:, pages, t] = m.transpose(1, 0, 2)
+            ov[:, pages, t] = np.where(m, x, np.float16(0)).transpose(1, 0, 2)
 
     # -- canonical outlier listing, the form parity tests compare --
     def outlier_entries(self, layer, h, page, kv):
         """Sorted (slot, d, fp16 bits) tuples of one page segment."""
-        out = []
-        for (hh, pg, k, s), (d, v) in self.rows[layer].items():
-            if hh == h and pg == page and k == kv:
-                bits = v.view(np.uint16)
-                out.extend((s, int(dd), int(bb)) for dd, bb in zip(d, bits))
-        return sorted(out)
+        if self.outm[layer][kv] is None:
+            return []
+        m = self.outm[layer][kv][h, page]
+        s, d = np.nonzero(m)
+        bits = self.outv[layer][kv][h, page][s, d].view(np.uint16)
+        return sorted(zip(s.tolist(), d.tolist(), bits.tolist()))
+
+    def outlier_array(self, layer):
+        """Every outlier as rows (h, page, kv, slot, d, fp16 bits), sorted."""
+        parts = []
+        for kv in range(2):
+            if self.outm[layer][kv] is None:
+                continue
+            h, b, s, d = np.nonzero(self.outm[layer][kv])
+            bits = self.outv[layer][kv][h, b, s, d].view(np.uint16).astype(np.int64)
+            parts.append(np.stack([h, b, np.full_like(h, kv), s, d, bits], axis=1))
+        if not parts:
+            return np.zeros((0, 6), np.int64)
+        a = np.concatenate(parts).astype(np.int64)
+        return a[np.lexsort(a.T[::-1])]
 
     # -- dequantise (compact_pool.py:293-395) --
-    def dequant_page(self, layer, h, page, first_pos):
-        """(K, V) fp16 arrays (S, D) of one page for head h.
-
-        ``first_pos`` is the absolute position of slot 0 (V tail clamp,
-        compact_pool.py:370-372).
-        """
+    def dequant_pages(self, layer, pages, first_pos):
+        """(K, V) fp16 (H, P, S, D) of pool pages ``pages`` whose slot 0 sits
+        at absolute position ``first_pos`` (V tail clamp, compact_pool.py:370-372)."""
         sc = self.scales[layer]
-        kc = unpack_codes(self.codes[layer][0][h, page], sc.bits_k).astype(np.int64)   # (S, D)
-        vc = unpack_codes(self.codes[layer][1][h, page], sc.bits_v).astype(np.int64)
-        k = np.take_along_axis(np.broadcast_to(sc.k_poles[h][None], (self.S, self.D, sc.k_poles.shape[-1])),
-                               kc[..., None], axis=-1)[..., 0].astype(np.float16)
-        p = np.minimum(first_pos + np.arange(self.S), sc.t_cal - 1)
-        vpol = sc.v_poles[h, p]                                                     # (S, L)
-        v = np.take_along_axis(vpol[:, None, :].repeat(self.D, 1), vc[..., None], axis=-1)[..., 0]
-        v = v.astype(np.float16)
-        for s in range(self.S):
-            for kv, arr in ((0, k), (1, v)):
-                r = self.rows[layer].get((h, int(page), kv, s))
-                if r is not None and r[0].size:
-                    arr[s, r[0].astype(np.int64)] = r[1]
+        pages = np.asarray(pages, np.int64)
+        first_pos = np.asarray(first_pos, np.int64)
+        kc = unpack_codes(self.codes[layer][0][:, pages], sc.bits_k)                # (H, P, S, D)
+        vc = unpack_codes(self.codes[layer][1][:, pages], sc.bits_v)
+        k = np.take_along_axis(sc.k_poles[:, None, None, :, :], kc[..., None].astype(np.intp), axis=-1)[..., 0]
+        p = np.minimum(first_pos[:, None] + np.arange(self.S)[None], sc.t_cal - 1)  # (P, S)
+        vpol = sc.v_poles[:, p]                                                    # (H, P, S, L)
+        v = np.take_along_axis(vpol[:, :, :, None, :], vc[..., None].astype(np.intp), axis=-1)[..., 0]
+        k, v = k.astype(np.float16), v.astype(np.float16)
+        for kv, arr in ((0, k), (1, v)):
+            if self.outm[layer][kv] is not None:
+                m = self.outm[layer][kv][:, pages]
+                arr[m] = self.outv[layer][kv][:, pages][m]
         return k, v
+
+    def dequant_page(self, layer, h, page, first_pos):
+        """(K, V) fp16 arrays (S, D) of one page for head h."""
+        k, v = self.dequant_pages(layer, [page], [first_pos])
+        return k[h, 0], v[h, 0]
 
     def unpack_to_staging(self, layer, block_ids, first_pos):
         """(NK, S, H, D) fp16 staging for K and V (compact_pool.py:492-537)."""
-        nk = len(block_ids)
-        sk = np.zeros((nk, self.S, self.H, self.D), np.float16)
-        sv = np.zeros_like(sk)
-        for i, (b, fp) in enumerate(zip(block_ids, first_pos)):
-            for h in range(self.H):
-                k, v = self.dequant_page(layer, h, int(b), int(fp))
-                sk[i, :, h] = k
-                sv[i, :, h] = v
-        return sk, sv
+        k, v = self.dequant_pages(layer, block_ids, first_pos)
+        return k.transpose(1, 2, 0, 3).copy(), v.transpose(1, 2, 0, 3).copy()
 
-    def dequant_sequence(self, layer, block_table, n_tokens, page_offset=0, v_pos="logical"):
+    def dequant_sequence(self, layer, block_table, n_tokens, page_offset=0, v_pos="logical", chunk=1024):
         """Dequantised (n_tokens, H, D) K and V of one sequence.
 
         Logical page j lives in pool page ``block_table[j]`` and starts at
@@ -180,12 +214,48 @@ class OraclePool:
         compact_pool.py:370-372).
         """
         n_pages = -(-n_tokens // self.S)
+        bt = np.asarray(block_table, np.int64)[:n_pages]
+        first = (bt if v_pos == "physical" else np.arange(n_pages)) + page_offset
         K = np.zeros((n_pages * self.S, self.H, self.D), np.float16)
         V = np.zeros_like(K)
-        for j in range(n_pages):
-            for h in range(self.H):
-                first = int(block_table[j]) if v_pos == "physical" else j
-                k, v = self.dequant_page(layer, h, int(block_table[j]), (page_offset + first) * self.S)
-                K[j * self.S:(j + 1) * self.S, h] = k
-                V[j * self.S:(j + 1) * self.S, h] = v
+        for a in range(0, n_pages, chunk):
+            b = min(a + chunk, n_pages)
+            k, v = self.dequant_pages(layer, bt[a:b], first[a:b] * self.S)
+            K[a * self.S:b * self.S] = k.transpose(1, 2, 0, 3).reshape(-1, self.H, self.D)
+            V[a * self.S:b * self.S] = v.transpose(1, 2, 0, 3).reshape(-1, self.H, self.D)
         return K[:n_tokens], V[:n_tokens]
+
+
+def dequant_packed_pages(k_rows, v_rows, dir_h, arena, pages, first_pos, k_poles_h, v_poles_h, bits_k, bits_v):
+    """Decode pages of one head straight from the packed pool format.
+
+    ``k_rows`` / ``v_rows`` (NB, S, RB) uint8 code rows of head h, ``dir_h``
+    (NB, 2, 4) directory records {offset, capacity, count, rows}, ``arena``
+    the layer's entries (fp16 value | channel << 16 | slot << 24), ``pages``
+    the pool pages to decode with the absolute position of their slot 0 in
+    ``first_pos``; poles of head h: K (D, Lk), V (t_cal, Lv). Returns K, V
+    (m, S, D) fp16 (compact_pool.py:293-395, V rows clamped at t_cal - 1).
+    """
+    pages = np.asarray(pages, np.int64)
+    first_pos = np.asarray(first_pos, np.int64)
+    kc = unpack_codes(k_rows[pages], bits_k).astype(np.intp)                     # (m, S, D)
+    vc = unpack_codes(v_rows[pages], bits_v).astype(np.intp)
+    m, S, D = kc.shape
+    K = np.take_along_axis(np.asarray(k_poles_h)[None, None], kc[..., None], axis=-1)[..., 0]
+    t_cal = v_poles_h.shape[0]
+    pos = np.minimum(first_pos[:, None] + np.arange(S)[None], t_cal - 1)         # (m, S)
+    V = np.take_along_axis(np.asarray(v_poles_h)[pos][:, :, None, :], vc[..., None], axis=-1)[..., 0]
+    K, V = K.astype(np.float16), V.astype(np.float16)
+    arena = np.asarray(arena).astype(np.int64) & 0xFFFFFFFF
+    for kv, arr in ((0, K), (1, V)):
+        rec = np.asarray(dir_h)[pages, kv].astype(np.int64)                      # (m, 4)
+        off, cnt = rec[:, 0], rec[:, 2]
+        tot = int(cnt.sum())
+        if tot == 0:
+            continue
+        which = np.repeat(np.arange(m), cnt)
+        start = np.repeat(np.cumsum(cnt) - cnt, cnt)
+        e = arena[np.repeat(off, cnt) + np.arange(tot) - start]
+        slot, ch = (e >> 24) & 31, (e >> 16) & 255
+        arr[which, slot, ch] = (e & 0xFFFF).astype(np.uint16).view(np.float16)
+    return K, V

@@ -42,28 +42,36 @@ def gpu_codes(gpu, layer):
     return c[:, :, :S * rbk].reshape(H, NB, S, rbk), c[:, :, S * rbk:].reshape(H, NB, S, rbv)
 
 
+def gpu_outlier_array(gpu, layer):
+    """Every outlier entry of the GPU pool as rows (h, page, kv, slot, d,
+    fp16 bits), sorted; the order inside a page list is not part of the format."""
+    lay = gpu.layers[layer]
+    d = np16(lay.dir).astype(np.int64)                        # (H, NB, 2, 4)
+    arena = np16(lay.arena).astype(np.int64) & 0xFFFFFFFF
+    off, cnt = d[..., 0].reshape(-1), d[..., 2].reshape(-1)
+    if cnt.sum() == 0:
+        return np.zeros((0, 6), np.int64)
+    rec = np.repeat(np.arange(off.size), cnt)
+    start = np.repeat(np.cumsum(cnt) - cnt, cnt)
+    e = arena[np.repeat(off, cnt) + np.arange(cnt.sum()) - start]
+    H, NB = d.shape[:2]
+    h, rest = np.divmod(rec, NB * 2)
+    b, kv = np.divmod(rest, 2)
+    a = np.stack([h, b, kv, (e >> 24) & 31, (e >> 16) & 255, e & 0xFFFF], axis=1)
+    return a[np.lexsort(a.T[::-1])]
+
+
+def _sets(a):
+    out = {}
+    for h, b, kv, s, d, bits in a.tolist():
+        out.setdefault((h, b, kv), []).append((s, d, bits))
+    return {k: sorted(v) for k, v in out.items()}
+
+
 def gpu_outlier_sets(gpu, layer):
     """{(h, page, kv): sorted [(slot, d, bits)]} for every non-empty list."""
-    lay = gpu.layers[layer]
-    d = np16(lay.dir).astype(np.int64)
-    arena = np16(lay.arena).astype(np.int64) & 0xFFFFFFFF
-    out = {}
-    H, NB = d.shape[:2]
-    for h in range(H):
-        for b in range(NB):
-            for kv in range(2):
-                off, _cap, cnt, _rows = d[h, b, kv]
-                if cnt:
-                    e = arena[off:off + cnt]
-                    out[(h, b, kv)] = sorted(zip(((e >> 24) & 31).tolist(), ((e >> 16) & 255).tolist(),
-                                                 (e & 0xFFFF).tolist()))
-    return out
+    return _sets(gpu_outlier_array(gpu, layer))
 
 
 def oracle_outlier_sets(orc, layer):
-    out = {}
-    for (h, pg, kv, s), (d, v) in orc.rows[layer].items():
-        if d.size:
-            out.setdefault((h, pg, kv), []).extend(
-                (s, int(dd), int(bb)) for dd, bb in zip(d, v.view(np.uint16)))
-    return {k: sorted(v) for k, v in out.items()}
+    return _sets(orc.outlier_array(layer))

@@ -127,6 +127,85 @@ def test_pool_config1_bit_exact(layout):
     assert 0.005 * T * H * D * 2 < n_out < 0.1 * T * H * D * 2
 
 
+def _adversarial_codebooks(L):
+    """Codebook rows (fp16) that stress the bisection path of the pack kernel:
+    regular, tiny gaps, duplicates, unsorted, subnormal, huge spread, a
+    non-finite pole, all equal."""
+    from kvquant.synthetic import codebook
+    z = codebook(L, "cpu").numpy().astype(np.float64)
+    rng = np.random.default_rng(L)
+    rows = [z, z * 1e-3, np.repeat(z[::2], 2)[:L], rng.permutation(z),
+            np.arange(L) * 6e-8 - 6e-8 * (L // 2), np.sign(z) * np.abs(z) ** 4 * 6e4 / np.abs(z).max() ** 4,
+            np.where(np.arange(L) == L - 1, np.inf, z), np.full(L, 0.5)]
+    if L == 4:
+        rows[5] = np.array([-6e4, -1e-3, 1e-3, 6e4])
+        rows[6] = np.array([-1.0, 0.0, np.nan, 1.0])
+    return np.stack([np.asarray(r, np.float64).astype(np.float16) for r in rows])  # (8, L)
+
+
+@pytest.mark.parametrize("levels", [16, 4])
+def test_pool_codes_exhaustive_fp16_adversarial_codebooks(levels):
+    """Every fp16 bit pattern (finite, subnormal, +-inf, NaN) through the pool
+    pack under eight kinds of codebook, for K (per-channel rows) and V
+    (per-token rows): codes, outlier lists and page stats bit-exact against
+    the reference's fp32 scan (oracle)."""
+    from kvquant.scales import KVScales, PerChannelScale, PerTokenScale
+    H, D, S, T = 4, 128, 16, 1024
+    books = _adversarial_codebooks(levels)                       # (8, L)
+    # K: channel (h, d) uses book (h * D + d) % 8; its 64 channels share x patterns
+    kidx = (np.arange(H * D) % 8).reshape(H, D)
+    k_poles = books[kidx]                                        # (H, D, L)
+    jj = (np.arange(H * D) // 8).reshape(H, D)                   # index among its book's channels
+    kbits = (np.arange(T)[:, None, None] * 64 + jj[None]).astype(np.uint16)   # (T, H, D)
+    # V: token row (h, t) uses book t % 8; rows of one book cover every pattern
+    v_poles = books[np.broadcast_to(np.arange(T) % 8, (H, T))]   # (H, T, L)
+    vbits = ((((np.arange(T) // 8)[:, None, None] * H + np.arange(H)[None, :, None]) * D)
+             + np.arange(D)[None, None, :]).astype(np.uint16)
+    big = np.float16(65504.0)
+    sc = KVScales([PerChannelScale(torch.from_numpy(k_poles).cuda(), torch.full((H, D), big).cuda(),
+                                   torch.full((H, D), -big).cuda())],
+                  [PerTokenScale(torch.from_numpy(v_poles.copy()).cuda(), torch.full((H, T), big).cuda(),
+                                 torch.full((H, T), -big).cuda())])
+    K = torch.from_numpy(kbits.view(np.float16)).cuda()
+    V = torch.from_numpy(vbits.view(np.float16)).cuda()
+    gpu, orc = make_pools(sc, T // S, S, H, D, outlier_frac=0.05)
+    slots = torch.arange(T, device="cuda")
+    write_both(gpu, orc, 0, K, V, slots, slots)
+    gpu.check()
+    for a, b in zip(gpu_codes(gpu, 0), orc.codes[0]):
+        np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(np16(gpu.layers[0].stats).view(np.uint16), orc.stats[0].view(np.uint16))
+    assert gpu_outlier_sets(gpu, 0) == oracle_outlier_sets(orc, 0)
+
+
+@pytest.mark.parametrize("layout", ["nuq4", "nuq2"])
+def test_pool_slots_in_any_order(layout):
+    """Tokens of a page need not be contiguous in the input: slots [5, 3, 4,
+    20] (two runs on page 0), then a whole 64-page prefill in a random slot
+    order (each page written by many runs in one call). Same bytes as the
+    oracle, which writes the tokens one by one."""
+    from kvquant.synthetic import NUQ2, NUQ4, make_kv, make_scales
+    lay = {"nuq4": [NUQ4], "nuq2": [NUQ2]}[layout]
+    H, D, S = 4, 128, 16
+    sc = make_scales(lay, H, D, t_cal=512, seed=11)
+    # pages grown by many small runs double their lists repeatedly: room for that
+    gpu, orc = make_pools(sc, 70, S, H, D, outlier_frac=1.0)
+    K, V = make_kv(1024 + 4, H, D, seed=12, outlier_frac=lay[0][1] * 4, chan_seed=11)
+    s = torch.tensor([5, 3, 4, 20], device="cuda")
+    write_both(gpu, orc, 0, K[:4].contiguous(), V[:4].contiguous(), s, s)
+    g = torch.Generator(device="cuda").manual_seed(13)
+    perm = torch.randperm(1024, generator=g, device="cuda") + 5 * S
+    write_both(gpu, orc, 0, K[4:].contiguous(), V[4:].contiguous(), perm, perm)
+    gpu.check()
+    for a, b in zip(gpu_codes(gpu, 0), orc.codes[0]):
+        np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(np16(gpu.layers[0].stats).view(np.uint16), orc.stats[0].view(np.uint16))
+    assert gpu_outlier_sets(gpu, 0) == oracle_outlier_sets(orc, 0)
+    last = np16(gpu.layers[0].dir)[..., 3].view(np.uint32)      # (H, NB, 2)
+    assert (last[..., 0] & 0x80000000 == 0).all()                # every page lock released
+    assert (last[..., 1] == 0).all()                             # every per-launch run count back to 0
+
+
 def test_pool_incremental_appends_and_overwrite():
     """Decode-style one-token appends, a chunk straddling pages, skipped (-1)
     slots, an overwrite of a written slot, a sequence starting mid-page, and
