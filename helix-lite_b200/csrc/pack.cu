@@ -172,14 +172,15 @@ HX_DEVINL void atomic_max_f16(uint16_t* addr, uint16_t v, uint32_t* err) {
   set_err(err, HX_DEV_ERR_TIMEOUT);
 }
 
-// Write one packed code row from the warp's staged byte codes.
-HX_DEVINL void store_row(uint8_t* dst, const uint8_t* codes, int D, int bits) {
+// Write slot t's packed codes from the warp's staged byte codes into a
+// column-major block (byte j of slot t at j * S + t).
+HX_DEVINL void store_row(uint8_t* block, int t, int S, const uint8_t* codes, int D, int bits) {
   const int per = 8 / bits;
   const int nbytes = D / per;
   for (int b = lane_id(); b < nbytes; b += 32) {
     uint32_t v = 0;
     for (int j = 0; j < per; ++j) v |= (uint32_t)(codes[b * per + j] & ((1 << bits) - 1)) << (bits * j);
-    dst[b] = (uint8_t)v;
+    block[(int64_t)b * S + t] = (uint8_t)v;
   }
 }
 
@@ -267,14 +268,12 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
   {
     uint32_t* dk = dir_ptr(pool, h, pg, 0);
     uint32_t* dv = dir_ptr(pool, h, pg, 1);
-    // rows (slots written) live in the K record; the V record's last word is
-    // the bandwidth kernel's per-launch run count, zero between launches
-    LKs = {__ldcg(dk), __ldcg(dk + 1), __ldcg(dk + 2), __ldcg(dk + 3) & ~kGenericPageLock};
-    LVs = {__ldcg(dv), __ldcg(dv + 1), __ldcg(dv + 2), 0u};
-    if ((int)LKs.rows > t0) {
-      LKs.cnt = filter_slots(pool.arena, LKs.off, LKs.cnt, t0, t0 + n);
-      LVs.cnt = filter_slots(pool.arena, LVs.off, LVs.cnt, t0, t0 + n);
-    }
+    // a record's last word: rows (bits 0-7, slots written) | the bandwidth
+    // kernels' per-launch run count (bits 8-30, zero between launches) | lock (31)
+    LKs = {__ldcg(dk), __ldcg(dk + 1), __ldcg(dk + 2), __ldcg(dk + 3) & 0xFFu};
+    LVs = {__ldcg(dv), __ldcg(dv + 1), __ldcg(dv + 2), __ldcg(dv + 3) & 0xFFu};
+    if ((int)LKs.rows > t0) LKs.cnt = filter_slots(pool.arena, LKs.off, LKs.cnt, t0, t0 + n);
+    if ((int)LVs.rows > t0) LVs.cnt = filter_slots(pool.arena, LVs.off, LVs.cnt, t0, t0 + n);
   }
 
   // Count the run's outliers first and size the page lists once, so a
@@ -325,7 +324,7 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
       m[k] = __ballot_sync(0xffffffffu, out);
     }
     __syncwarp();
-    store_row(seg + (int64_t)t * rbk, sc8, D, pool.bits_k);
+    store_row(seg, t, S, sc8, D, pool.bits_k);
     append_row<KD>(pool, LKs, m, xb, t, err);
     __syncwarp();
 
@@ -353,7 +352,7 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
       m[k] = __ballot_sync(0xffffffffu, out);
     }
     __syncwarp();
-    store_row(seg + (int64_t)S * rbk + (int64_t)t * rbv, sc8, D, pool.bits_v);
+    store_row(seg + (int64_t)S * rbk, t, S, sc8, D, pool.bits_v);
     append_row<KD>(pool, LVs, m, xb, t, err);
     __syncwarp();
   }
@@ -375,7 +374,7 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
     uint32_t* dk = dir_ptr(pool, h, pg, 0);
     uint32_t* dv = dir_ptr(pool, h, pg, 1);
     dk[0] = LKs.off; dk[1] = LKs.cap; dk[2] = LKs.cnt;
-    dv[0] = LVs.off; dv[1] = LVs.cap; dv[2] = LVs.cnt;
+    dv[0] = LVs.off; dv[1] = LVs.cap; dv[2] = LVs.cnt; dv[3] = max(LVs.rows, rows_new);
     __threadfence();
     atomicExch(dk + 3, max(LKs.rows, rows_new));  // rows, lock bit clear
   }
@@ -384,9 +383,10 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
 // ---------------------------------------------------------------------------
 // staging unpack: one block per (selected page, head)
 
-HX_DEVINL int code_at(const uint8_t* rowp, int d, int bits) {
+// Code of channel d, slot t in a column-major block of S slots.
+HX_DEVINL int code_at(const uint8_t* block, int S, int t, int d, int bits) {
   const int per = 8 / bits;
-  return (rowp[d / per] >> ((d % per) * bits)) & ((1 << bits) - 1);
+  return (block[(d / per) * S + t] >> ((d % per) * bits)) & ((1 << bits) - 1);
 }
 
 __global__ void __launch_bounds__(128) unpack_pages_kernel(hx_pool_layer pool, hx_layer_scales sc,
@@ -408,8 +408,8 @@ __global__ void __launch_bounds__(128) unpack_pages_kernel(hx_pool_layer pool, h
   uint16_t* tv = tile + S * D;
   for (int e = threadIdx.x; e < S * D; e += blockDim.x) {
     int t = e / D, d = e % D;
-    int ck = code_at(seg + t * rbk, d, pool.bits_k);
-    int cv = code_at(seg + S * rbk + t * rbv, d, pool.bits_v);
+    int ck = code_at(seg, S, t, d, pool.bits_k);
+    int cv = code_at(seg + S * rbk, S, t, d, pool.bits_v);
     // a code >= levels can only come from an unwritten slot; it reads level 0
     ck = ck < sc.levels_k ? ck : 0;
     cv = cv < sc.levels_v ? cv : 0;

@@ -95,6 +95,50 @@ __global__ void scales_prepare_kernel(int mode, const uint16_t* poles, int64_t r
   }
 }
 
+// Decode tables of one layer, per KV head 96 KB laid out exactly as the decode
+// kernel keeps them in shared memory (24576 words):
+//   words [0, 16384): K, 256 rows (code byte b) x 64 words. nuq4: word 64 b + P
+//     = levels of channels 2P, 2P+1 for the two nibbles of b (pair tables, one
+//     per channel pair in its own bank column); nuq2: words 64 b + 2Q, +1 =
+//     levels of channels 4Q .. 4Q+3 for the four crumbs of b (quad tables).
+//   words [16384, 24576): V beyond t_cal (row t_cal - 1 of every token), 256
+//     rows x 32 words, the byte's levels replicated: nuq4 32 copies of the
+//     pair entry, nuq2 16 copies of the 8-byte quad entry.
+// Codes at or above a table's level count read 0.
+constexpr int kDecTabWords = 24576, kDecKWords = 16384;
+
+HX_DEVINL uint16_t pole_or0(const uint16_t* row, int L, int c) { return c < L ? row[c] : (uint16_t)0; }
+
+__global__ void decode_tables_kernel(const hx_layer_scales sc, int H, int bits_k, int bits_v, uint32_t* tabs) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)H * kDecTabWords) return;
+  const int h = (int)(idx / kDecTabWords), w = (int)(idx % kDecTabWords);
+  uint32_t v;
+  if (w < kDecKWords) {
+    const int b = w >> 6, col = w & 63;
+    const int Lk = sc.levels_k;
+    const uint16_t* kp = sc.k_poles + (int64_t)h * 128 * Lk;
+    if (bits_k == 4) {  // pair col: channels 2 col, 2 col + 1
+      v = pack_u16x2(pole_or0(kp + (2 * col) * Lk, Lk, b & 15), pole_or0(kp + (2 * col + 1) * Lk, Lk, b >> 4));
+    } else {            // quad col >> 1: channels 4q .. 4q+3, word half col & 1
+      const int q = col >> 1, e = col & 1;
+      v = pack_u16x2(pole_or0(kp + (4 * q + 2 * e) * Lk, Lk, (b >> (4 * e)) & 3),
+                     pole_or0(kp + (4 * q + 2 * e + 1) * Lk, Lk, (b >> (4 * e + 2)) & 3));
+    }
+  } else {
+    const int r = w - kDecKWords, b = r >> 5, col = r & 31;
+    const int Lv = sc.levels_v;
+    const uint16_t* vt = sc.v_poles + ((int64_t)h * sc.t_cal + (sc.t_cal - 1)) * Lv;
+    if (bits_v == 4) {
+      v = pack_u16x2(pole_or0(vt, Lv, b & 15), pole_or0(vt, Lv, b >> 4));
+    } else {
+      const int e = col & 1;
+      v = pack_u16x2(pole_or0(vt, Lv, (b >> (4 * e)) & 3), pole_or0(vt, Lv, (b >> (4 * e + 2)) & 3));
+    }
+  }
+  tabs[idx] = v;
+}
+
 // ---- fp16-pair helpers ---------------------------------------------------------
 
 HX_DEVINL uint32_t as_u32(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
@@ -152,6 +196,16 @@ HX_DEVINL int scan_code(float x, const uint16_t* poles, int L, float& pole) {
   pole = bp;
   return idx;
 }
+
+// Asynchronous 16- / 8-byte copies global -> shared (no registers held).
+HX_DEVINL void cp_async_16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+HX_DEVINL void cp_async_8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+HX_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+HX_DEVINL void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 HX_DEVINL uint16_t half_of(uint32_t v, int e) { return (uint16_t)(e ? (v >> 16) : (v & 0xFFFFu)); }
 
@@ -226,24 +280,15 @@ HX_DEVINL void lists_reserve(const hx_pool_layer& pool, ListRec& A, uint32_t nee
   __syncwarp();
 }
 
-// fp16 of channel 4 lane + k of batch token j from the K registers (static
+// fp16 of channel 4 lane + k of batch token j from the registers (static
 // indexing: a select per token keeps the array in registers)
-HX_DEVINL uint16_t kval8(const uint2 (&xk)[8], int j, int k) {
+template <int BT>
+HX_DEVINL uint16_t kval_batch(const uint2 (&xk)[BT], int j, int k) {
   uint32_t w = 0;
 #pragma unroll
-  for (int jj = 0; jj < 8; ++jj)
+  for (int jj = 0; jj < BT; ++jj)
     if (jj == j) w = k < 2 ? xk[jj].x : xk[jj].y;
   return half_of(w, k & 1);
-}
-
-// fp16 of channel b of this lane's V half row
-HX_DEVINL uint16_t vval(const uint4 (&xv)[8], int b) {
-  const int u = b >> 3, comp = (b >> 1) & 3;
-  uint32_t w = 0;
-#pragma unroll
-  for (int uu = 0; uu < 8; ++uu)
-    if (uu == u) w = comp == 0 ? xv[uu].x : comp == 1 ? xv[uu].y : comp == 2 ? xv[uu].z : xv[uu].w;
-  return half_of(w, b & 1);
 }
 
 HX_DEVINL int warp_excl_scan(int v, int& total) {
@@ -276,33 +321,76 @@ HX_DEVINL bool page_lock(uint32_t* rows_word, uint32_t* err) {
   return __shfl_sync(0xffffffffu, got, 0) != 0;
 }
 
-// ---- the kernel -----------------------------------------------------------------
-//
-// One warp per (window of 16 input tokens, head). A run is a maximal stretch
-// of input tokens filling consecutive slots of one page; each run starting in
-// the window is processed whole (it may reach past the window's end). Tokens of
-// a page may come in any order: a page that gets several runs in one launch is
-// updated by one run at a time (page lock), so no list entry or stat is lost.
-//
-// K: lane l owns channels 4l .. 4l+3 over the run's tokens (thresholds per
-// channel pair in registers; one 8-byte load per token row). V: lane l owns
-// half a row (64 channels) of slot l >> 1 (the row's thresholds in registers;
-// eight 16-byte loads, one or two 16-byte code stores).
-constexpr int PF_D = 128, PF_S = 16;
-constexpr int PF_STAGE = 512;  // outlier entries of one run staged in shared memory (more go direct)
+// Elements of one token's 4 channels (pairs xa, xb) outside the fast range:
+// the reference's scan. Returns the code pairs with the scanned codes patched
+// in, and per channel the pole a scanned K non-outlier reconstructs to (NaN
+// where there is none; it enters the K stats). Out of line: rarely taken.
+struct ScanFix {
+  uint32_t ca, cb;
+  float p0, p1, p2, p3;
+};
 
-template <int BK, int BV>
-__global__ void __launch_bounds__(128, 4)
-    pack_fast_kernel(const hx_pool_layer pool, const hx_layer_scales sc, const uint16_t* __restrict__ key,
-                     const uint16_t* __restrict__ value, const int64_t* __restrict__ slots,
-                     const int64_t* __restrict__ abspos, int T, uint32_t* err) {
-  constexpr int RBK = PF_D * BK / 8, RBV = PF_D * BV / 8;  // code bytes per token row
-  constexpr int SEG = PF_S * (RBK + RBV);
-  __shared__ uint32_t s_ent[4][PF_STAGE];  // a run's outlier entries, K's then V's
-  const int lane = lane_id();
-  uint32_t* sent = s_ent[threadIdx.x >> 5];
+// Channel k's poles are at pbase + k * pstride (K: one row per channel; V: the
+// token's row, pstride 0).
+__device__ __noinline__ ScanFix scan_fix(const uint16_t* pbase, int pstride, int L, uint32_t xa, uint32_t xb,
+                                         uint32_t sa, uint32_t sb, uint32_t oa, uint32_t ob, uint32_t ca,
+                                         uint32_t cb) {
+  float pl[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    pl[k] = __int_as_float(0x7fc00000);
+    const uint32_t sm = k < 2 ? sa : sb;
+    if (half_of(sm, k & 1)) {
+      const float xv = h2f(half_of(k < 2 ? xa : xb, k & 1));
+      float pole;
+      const int c = scan_code(xv, pbase + k * pstride, L, pole);
+      const uint32_t sh = (k & 1) ? 16u : 0u;
+      if (k < 2) ca = (ca & ~(0xFu << sh)) | ((uint32_t)c << sh);
+      else cb = (cb & ~(0xFu << sh)) | ((uint32_t)c << sh);
+      if (!half_of(k < 2 ? oa : ob, k & 1)) pl[k] = pole;
+    }
+  }
+  return {ca, cb, pl[0], pl[1], pl[2], pl[3]};
+}
+
+// ---- the kernels ----------------------------------------------------------------
+//
+// Two launches per call, one per list kind (K, then V), after a pre-pass that
+// counts the runs each (head, page) receives. One warp per (window of 16
+// input tokens, head). A run is a maximal stretch of input tokens filling
+// consecutive slots of one page; each run starting in the window is processed
+// whole (it may reach past the window's end). Lane l owns channels 4l .. 4l+3
+// of every token of the run: one 8-byte load per token row, codes by
+// bisection (K: the thresholds of the lane's channel pairs in registers; V:
+// each token's row of thresholds from shared memory), and the lane's byte
+// column(s) of the page's column-major code block (nuq4: pairs 2l and 2l+1,
+// nuq2: quad l) written as one 16-byte store per column for a whole page.
+//
+// Each directory record's last word is rows (bits 0-7, slots written) |
+// runs (bits 8-30, this launch's run count from the pre-pass) | lock (bit
+// 31). A page with one run belongs to its warp: record and stats are read
+// beside the data loads and written back plainly. A page with several runs
+// (tokens of the page not contiguous in the input) is updated one run at a
+// time under the record's lock, so no list entry or stat is lost.
+constexpr int PF_D = 128, PF_S = 16;
+constexpr int PF_STAGE = PF_S * PF_D;  // one run's outlier entries, staged (every element at worst)
+constexpr uint32_t kRunsOne = 1u << 8, kRunsMask = 0x7FFFFF00u, kRowsMask = 0xFFu;
+
+template <int BITS, bool IS_V>
+__global__ void __launch_bounds__(128, IS_V ? 5 : 4)
+    pack_list_kernel(const hx_pool_layer pool, const hx_layer_scales sc, const uint16_t* __restrict__ x,
+                     const int64_t* __restrict__ slots, const int64_t* __restrict__ abspos, int T, uint32_t* err) {
+  // tokens per batch: K's nuq4 thresholds take 32 registers, so fewer tokens in flight
+  constexpr int BT = (!IS_V && BITS == 4) ? 4 : 8;
+  __shared__ uint32_t s_ent[4][PF_STAGE];                  // a run's outlier entries
+  __shared__ __align__(16) uint32_t s_pre[4][4 + 4 * 32];  // an exclusive page's record and stats
+  __shared__ __align__(16) uint32_t s_vt[IS_V ? 4 : 1][IS_V ? 16 * 20 : 1];  // V: per slot 16 thresholds + band (80-byte rows)
+  const int lane = lane_id(), warp = threadIdx.x >> 5;
+  uint32_t* sent = s_ent[warp];
   const int H = pool.num_kv_heads, NB = pool.num_blocks, Tc = sc.t_cal;
-  const int64_t wg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t seg_bytes = (int64_t)PF_S * PF_D * (pool.bits_k + pool.bits_v) / 8;
+  const int64_t blk_off = IS_V ? (int64_t)PF_S * PF_D * pool.bits_k / 8 : 0;
+  const int64_t wg = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
   const int64_t nwin = ((int64_t)T + 15) / 16;
   if (wg >= nwin * H) return;
   const int win = (int)(wg / H), h = (int)(wg % H);
@@ -322,8 +410,23 @@ __global__ void __launch_bounds__(128, 4)
   }
   uint32_t leaders = __ballot_sync(0xffffffffu, lead);
   if (!leaders) return;
+  const int L = IS_V ? sc.levels_v : sc.levels_k;
 
-  const int LK = sc.levels_k, LV = sc.levels_v;
+  // K: thresholds of channel pairs 2l, 2l+1 (channels 4l .. 4l+3) and the band
+  uint32_t ka[16], kb[16], kupa = 0, kupb = 0, kloa = 0, klob = 0;
+  if (!IS_V) {
+    const uint4* ta = reinterpret_cast<const uint4*>(sc.k_thresh) + ((int64_t)h * (PF_D / 2) + 2 * lane) * 4;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (BITS == 2 && q > 0 && q < 3) continue;
+      const uint4 a = __ldg(ta + q), b = __ldg(ta + 4 + q);
+      ka[4 * q] = a.x; ka[4 * q + 1] = a.y; ka[4 * q + 2] = a.z; ka[4 * q + 3] = a.w;
+      kb[4 * q] = b.x; kb[4 * q + 1] = b.y; kb[4 * q + 2] = b.z; kb[4 * q + 3] = b.w;
+    }
+    const uint2 u = *reinterpret_cast<const uint2*>(sc.k_upper + (int64_t)h * PF_D + 4 * lane);
+    const uint2 lo = *reinterpret_cast<const uint2*>(sc.k_lower + (int64_t)h * PF_D + 4 * lane);
+    kupa = u.x; kupb = u.y; kloa = lo.x; klob = lo.y;
+  }
 
   while (leaders) {
     const int r = __ffs(leaders) - 1;
@@ -343,313 +446,230 @@ __global__ void __launch_bounds__(128, 4)
       const uint32_t m = __ballot_sync(0xffffffffu, ok) | 1u;
       n = __ffs(~m) - 1;
     }
-    uint8_t* seg = pool.codes + ((int64_t)h * NB + pg) * SEG;
-    uint32_t* dk = pool.dir + (((int64_t)h * NB + pg) * 2 + 0) * 4;
-    uint32_t* dv = dk + 4;
+    uint8_t* blk = pool.codes + ((int64_t)h * NB + pg) * seg_bytes + blk_off;
+    uint32_t* rec = pool.dir + (((int64_t)h * NB + pg) * 2 + (IS_V ? 1 : 0)) * 4;
     uint16_t* st = pool.stats + ((int64_t)h * NB + pg) * 2 * PF_D + 4 * lane;
-    // A page that receives one run in this launch (the pre-pass counted the
-    // page's runs into the last word of its V record) belongs to this warp
-    // alone: its records and stats are read now, beside the data loads, and
-    // written back without a lock. A page with several runs is read and
-    // written under the page lock at the end.
-    const bool excl = __ldcg(dv + 3) == 1u;
-    uint4 rk = make_uint4(0u, 0u, 0u, 0u), rv = rk;
-    uint2 smin = make_uint2(0u, 0u), smax = smin;
+    const bool excl = (__ldcg(rec + 3) & kRunsMask) == kRunsOne;
+    // an exclusive page's record and stats are fetched now, into shared
+    // memory (no registers held across the compute)
+    uint32_t* s_rec = s_pre[warp];  // [0..3] record, [4 + 4 lane ..] stats min / max of the lane's channels
     if (excl) {
-      rk = __ldcg(reinterpret_cast<const uint4*>(dk));
-      rv = __ldcg(reinterpret_cast<const uint4*>(dv));
-      smin = __ldcg(reinterpret_cast<const uint2*>(st));
-      smax = __ldcg(reinterpret_cast<const uint2*>(st + PF_D));
+      if (lane == 0) cp_async_16(s_rec, rec);
+      if (!IS_V) {
+        cp_async_8(s_rec + 4 + 4 * lane, st);
+        cp_async_8(s_rec + 6 + 4 * lane, st + PF_D);
+      }
+      cp_async_commit();
+    }
+    if (IS_V) {
+      // thresholds and band of the run's V rows: lane 2j + e stages half of slot j's
+      __syncwarp();
+      const int j = lane >> 1, e = lane & 1;
+      if (j < n) {
+        int64_t p = abspos[i + j];
+        if (p < 0) {
+          set_err(err, HX_DEV_ERR_BOUNDS);
+          p = 0;
+        }
+        const int64_t rr = (int64_t)h * Tc + (p < Tc ? p : Tc - 1);
+        const uint4* tr = reinterpret_cast<const uint4*>(sc.v_thresh) + rr * 4 + 2 * e;
+        uint32_t* dstv = s_vt[warp] + j * 20;
+        const uint4 a = __ldg(tr), b = __ldg(tr + 1);
+        reinterpret_cast<uint4*>(dstv)[2 * e] = a;
+        reinterpret_cast<uint4*>(dstv)[2 * e + 1] = b;
+        if (e == 0) {
+          dstv[16] = (uint32_t)sc.v_upper[rr] * 0x00010001u;
+          dstv[17] = (uint32_t)sc.v_lower[rr] * 0x00010001u;
+        }
+      }
+      __syncwarp();
     }
 
-    // ---- K: issue the run's row loads, then code them token by token
-    // K tables of this lane's channel pairs 2l, 2l+1 (channels 4l .. 4l+3)
-    uint32_t ka[16], kb[16];
-    {
-      const uint4* ta = reinterpret_cast<const uint4*>(sc.k_thresh) + ((int64_t)h * (PF_D / 2) + 2 * lane) * 4;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (BK == 2 && q > 0 && q < 3) continue;
-        const uint4 a = __ldg(ta + q), b = __ldg(ta + 4 + q);
-        ka[4 * q] = a.x; ka[4 * q + 1] = a.y; ka[4 * q + 2] = a.z; ka[4 * q + 3] = a.w;
-        kb[4 * q] = b.x; kb[4 * q + 1] = b.y; kb[4 * q + 2] = b.z; kb[4 * q + 3] = b.w;
-      }
-    }
-    const uint32_t kxa = ka[15], kxb = kb[15];  // bounds of the fast path
-    uint32_t kupa, kupb, kloa, klob;
-    {
-      const uint2 u = *reinterpret_cast<const uint2*>(sc.k_upper + (int64_t)h * PF_D + 4 * lane);
-      const uint2 lo = *reinterpret_cast<const uint2*>(sc.k_lower + (int64_t)h * PF_D + 4 * lane);
-      kupa = u.x; kupb = u.y; kloa = lo.x; klob = lo.y;
-    }
-    uint32_t cmina = 0x001F001Fu, cminb = 0x001F001Fu, cmaxa = 0u, cmaxb = 0u;  // code range (+1 for max)
-    float emin[4], emax[4];  // outliers and scanned elements, exact values
+    uint32_t cmina = 0x001F001Fu, cminb = 0x001F001Fu, cmaxa = 0u, cmaxb = 0u;  // K code range (+1 for max)
+    float emin[4], emax[4];  // K outliers and scanned elements, exact values
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       emin[k] = __int_as_float(0x7f800000);
       emax[k] = __int_as_float(0xff800000);
     }
-    // two batches of 8 tokens: bit 4 jj + k of kout_b = channel 4 lane + k of
-    // token 8 b + jj is an outlier; its entry is staged at kbase_b + rank
-    uint32_t kout0 = 0, kout1 = 0;
-    int kbase0 = 0, kbase1 = 0, totk = 0;
+    uint32_t colA[4] = {0u, 0u, 0u, 0u}, colB[4] = {0u, 0u, 0u, 0u};  // byte j = run token j
+    // batches of BT tokens; a batch's outlier entries are staged (lane-major)
+    // after the previous batches' while its values are in registers
+    int tot = 0;
 #pragma unroll 1
-    for (int hb = 0; hb < 2; ++hb) {
-      const int j0 = 8 * hb;
+    for (int hb = 0; hb < PF_S / BT; ++hb) {
+      const int j0 = BT * hb;
       if (j0 >= n) break;
-      uint2 xk[8];
+      uint2 xs[BT];
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj)
-        xk[jj] = j0 + jj < n
-                     ? *reinterpret_cast<const uint2*>(key + ((int64_t)(i + j0 + jj) * H + h) * PF_D + 4 * lane)
-                     : make_uint2(0u, 0u);
-      uint32_t kout = 0;
+      for (int jj = 0; jj < BT; ++jj)
+        xs[jj] = j0 + jj < n ? *reinterpret_cast<const uint2*>(x + ((int64_t)(i + j0 + jj) * H + h) * PF_D + 4 * lane)
+                             : make_uint2(0u, 0u);
+      uint32_t outm = 0;
+      uint32_t wA[BT / 4], wB[BT / 4];  // the batch's column bytes (byte jj at word jj / 4)
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
+      for (int u = 0; u < BT / 4; ++u) wA[u] = wB[u] = 0u;
+#pragma unroll
+      for (int jj = 0; jj < BT; ++jj) {
         if (j0 + jj < n) {
-          const uint32_t xa = xk[jj].x, xb = xk[jj].y;
-          uint32_t ca = codes2<BK>(xa, ka), cb = codes2<BK>(xb, kb);
-          const uint32_t oa = gt2(xa, kupa) | lt2(xa, kloa), ob = gt2(xb, kupb) | lt2(xb, klob);
-          const uint32_t sa = geu2(xa, kxa), sb = geu2(xb, kxb);
-          if (__any_sync(0xffffffffu, (sa | sb) != 0u)) {
-            // elements outside the fast range: the reference's scan
+          const uint32_t xa = xs[jj].x, xb = xs[jj].y;
+          uint32_t ca, cb, oa, ob, sa, sb;
+          if (IS_V) {
+            const uint32_t* vr = s_vt[warp] + (j0 + jj) * 20;
+            uint32_t tv[16];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t sm = k < 2 ? sa : sb;
-              if (half_of(sm, k & 1)) {
-                const uint32_t xw = k < 2 ? xa : xb;
-                const float x = h2f(half_of(xw, k & 1));
-                float pole;
-                const int c = scan_code(x, sc.k_poles + ((int64_t)h * PF_D + 4 * lane + k) * LK, LK, pole);
-                const uint32_t sh = (k & 1) ? 16u : 0u;
-                if (k < 2) ca = (ca & ~(0xFu << sh)) | ((uint32_t)c << sh);
-                else cb = (cb & ~(0xFu << sh)) | ((uint32_t)c << sh);
-                const uint32_t om = k < 2 ? oa : ob;
-                if (!half_of(om, k & 1)) {  // a scanned non-outlier reconstructs to its pole
-                  emin[k] = fminf(emin[k], pole);
-                  emax[k] = fmaxf(emax[k], pole);
-                }
-              }
+            for (int q = 0; q < 4; ++q) {
+              if (BITS == 2 && q > 0 && q < 3) continue;
+              const uint4 a = reinterpret_cast<const uint4*>(vr)[q];
+              tv[4 * q] = a.x; tv[4 * q + 1] = a.y; tv[4 * q + 2] = a.z; tv[4 * q + 3] = a.w;
+            }
+            const uint32_t vup = vr[16], vlo = vr[17];
+            ca = codes2<BITS>(xa, tv);
+            cb = codes2<BITS>(xb, tv);
+            oa = gt2(xa, vup) | lt2(xa, vlo);
+            ob = gt2(xb, vup) | lt2(xb, vlo);
+            sa = geu2(xa, tv[15]);
+            sb = geu2(xb, tv[15]);
+          } else {
+            ca = codes2<BITS>(xa, ka);
+            cb = codes2<BITS>(xb, kb);
+            oa = gt2(xa, kupa) | lt2(xa, kloa);
+            ob = gt2(xb, kupb) | lt2(xb, klob);
+            sa = geu2(xa, ka[15]);
+            sb = geu2(xb, kb[15]);
+          }
+          if (__any_sync(0xffffffffu, (sa | sb) != 0u)) {
+            const uint16_t* pb;
+            if (IS_V) {
+              int64_t p = abspos[i + j0 + jj];
+              p = p < 0 ? 0 : p;
+              pb = sc.v_poles + ((int64_t)h * Tc + (p < Tc ? p : Tc - 1)) * L;
+            } else {
+              pb = sc.k_poles + ((int64_t)h * PF_D + 4 * lane) * L;
+            }
+            const ScanFix f = scan_fix(pb, IS_V ? 0 : L, L, xa, xb, sa, sb, oa, ob, ca, cb);
+            ca = f.ca;
+            cb = f.cb;
+            if (!IS_V) {  // fminf / fmaxf ignore the NaN of channels not scanned
+              emin[0] = fminf(emin[0], f.p0); emax[0] = fmaxf(emax[0], f.p0);
+              emin[1] = fminf(emin[1], f.p1); emax[1] = fmaxf(emax[1], f.p1);
+              emin[2] = fminf(emin[2], f.p2); emax[2] = fmaxf(emax[2], f.p2);
+              emin[3] = fminf(emin[3], f.p3); emax[3] = fmaxf(emax[3], f.p3);
             }
           }
-          // code range of the fast non-outlier elements
-          const uint32_t exa = oa | sa, exb = ob | sb;
-          cmina = umin2(cmina, ca | (exa & 0x001F001Fu));
-          cminb = umin2(cminb, cb | (exb & 0x001F001Fu));
-          cmaxa = umax2(cmaxa, (ca + 0x00010001u) & ~exa);
-          cmaxb = umax2(cmaxb, (cb + 0x00010001u) & ~exb);
-          kout |= ((oa & 1u) | ((oa >> 15) & 2u) | ((ob & 1u) << 2) | ((ob >> 13) & 8u)) << (4 * jj);
-          const int tt = t0 + j0 + jj;
-          if (BK == 4) {
-            const uint32_t w = (ca & 0xFu) | ((ca >> 12) & 0xF0u) | ((cb & 0xFu) << 8) | ((cb >> 4) & 0xF000u);
-            *reinterpret_cast<uint16_t*>(seg + tt * RBK + 2 * lane) = (uint16_t)w;
+          if (!IS_V) {  // code range of the fast non-outlier elements
+            const uint32_t exa = oa | sa, exb = ob | sb;
+            cmina = umin2(cmina, ca | (exa & 0x001F001Fu));
+            cminb = umin2(cminb, cb | (exb & 0x001F001Fu));
+            cmaxa = umax2(cmaxa, (ca + 0x00010001u) & ~exa);
+            cmaxb = umax2(cmaxb, (cb + 0x00010001u) & ~exb);
+          }
+          outm |= ((oa & 1u) | ((oa >> 15) & 2u) | ((ob & 1u) << 2) | ((ob >> 13) & 8u)) << (4 * jj);
+          const int sh = 8 * (jj & 3);
+          if (BITS == 4) {
+            wA[jj >> 2] |= ((ca & 0xFu) | ((ca >> 12) & 0xF0u)) << sh;
+            wB[jj >> 2] |= ((cb & 0xFu) | ((cb >> 12) & 0xF0u)) << sh;
           } else {
-            const uint32_t w = (ca & 3u) | ((ca >> 14) & 0xCu) | ((cb & 3u) << 4) | ((cb >> 10) & 0xC0u);
-            seg[tt * RBK + lane] = (uint8_t)w;
+            wA[jj >> 2] |= ((ca & 3u) | ((ca >> 14) & 0xCu) | ((cb & 3u) << 4) | ((cb >> 10) & 0xC0u)) << sh;
           }
         }
       }
-      // the batch's K entries (lane-major, then token, then channel) staged
-      // while the values are in registers; the outliers also enter the stats
+      // the batch's words into the run's columns (static indices: predicated moves)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int u = 0; u < BT / 4; ++u)
+          if (q == j0 / 4 + u) {
+            colA[q] = wA[u];
+            colB[q] = wB[u];
+          }
+      // the batch's entries (lane-major: channel group, then token, then
+      // channel) staged while the values are in registers; K's also enter
+      // the page stats
       int tb;
-      const int base = totk + warp_excl_scan(__popc(kout), tb);
+      const int base = tot + warp_excl_scan(__popc(outm), tb);
       {
-        uint32_t m = kout;
+        uint32_t m = outm;
         int q = base;
         while (m) {
           const int b = __ffs(m) - 1;
           m &= m - 1;
           const int jj = b >> 2, k = b & 3;
-          const uint16_t xb = kval8(xk, jj, k);
-          if (q < PF_STAGE)
-            sent[q] = (uint32_t)xb | ((uint32_t)(4 * lane + k) << 16) | ((uint32_t)(t0 + j0 + jj) << 24);
-          ++q;
-          const float x = h2f(xb);
+          const uint16_t xb = kval_batch<BT>(xs, jj, k);
+          sent[q++] = (uint32_t)xb | ((uint32_t)(4 * lane + k) << 16) | ((uint32_t)(t0 + j0 + jj) << 24);
+          if (!IS_V) {
+            const float xf = h2f(xb);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            if (kk == k) {
-              emin[kk] = fminf(emin[kk], x);
-              emax[kk] = fmaxf(emax[kk], x);
-            }
+            for (int kk = 0; kk < 4; ++kk)
+              if (kk == k) {
+                emin[kk] = fminf(emin[kk], xf);
+                emax[kk] = fmaxf(emax[kk], xf);
+              }
+          }
         }
       }
-      if (hb == 0) {
-        kout0 = kout;
-        kbase0 = base;
+      tot += tb;
+    }
+
+    // ---- the lane's byte columns of the code block
+    {
+      const int c0 = BITS == 4 ? 2 * lane : lane;
+      if (t0 == 0 && n == PF_S) {
+        reinterpret_cast<uint4*>(blk + c0 * PF_S)[0] = make_uint4(colA[0], colA[1], colA[2], colA[3]);
+        if (BITS == 4) reinterpret_cast<uint4*>(blk + (c0 + 1) * PF_S)[0] = make_uint4(colB[0], colB[1], colB[2], colB[3]);
       } else {
-        kout1 = kout;
-        kbase1 = base;
+#pragma unroll
+        for (int j = 0; j < PF_S; ++j)
+          if (j < n) {
+            blk[c0 * PF_S + t0 + j] = (uint8_t)(colA[j >> 2] >> (8 * (j & 3)));
+            if (BITS == 4) blk[(c0 + 1) * PF_S + t0 + j] = (uint8_t)(colB[j >> 2] >> (8 * (j & 3)));
+          }
       }
-      totk += tb;
     }
 
-    // ---- V: lane = (slot t, half row hf); the row's thresholds in registers
-    const int t = lane >> 1, hf = lane & 1;
-    const bool vact = t >= t0 && t < t0 + n;
-    const int iv = i + (t - t0);
-    uint64_t voutm = 0;
-    uint4 xv[8];
-    uint32_t tv[16], vup = 0, vlo = 0;
-    int vrow = 0;
-    if (vact) {
-      const uint4* src = reinterpret_cast<const uint4*>(value + ((int64_t)iv * H + h) * PF_D + 64 * hf);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) xv[u] = src[u];
-      int64_t p = abspos[iv];
-      if (p < 0) {
-        set_err(err, HX_DEV_ERR_BOUNDS);
-        p = 0;
+    // ---- the page's list (and K stats)
+    uint4 rc;
+    uint2 smin = make_uint2(0u, 0u), smax = smin;
+    if (excl) {
+      cp_async_wait_all();
+      __syncwarp();
+      rc = *reinterpret_cast<const uint4*>(s_rec);
+      if (!IS_V) {
+        smin = *reinterpret_cast<const uint2*>(s_rec + 4 + 4 * lane);
+        smax = *reinterpret_cast<const uint2*>(s_rec + 6 + 4 * lane);
       }
-      vrow = (int)(p < Tc ? p : Tc - 1);
-      const int64_t rr = (int64_t)h * Tc + vrow;
-      const uint4* tr = reinterpret_cast<const uint4*>(sc.v_thresh) + rr * 4;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (BV == 2 && q > 0 && q < 3) continue;
-        const uint4 a = __ldg(tr + q);
-        tv[4 * q] = a.x; tv[4 * q + 1] = a.y; tv[4 * q + 2] = a.z; tv[4 * q + 3] = a.w;
-      }
-      vup = (uint32_t)sc.v_upper[rr] * 0x00010001u;
-      vlo = (uint32_t)sc.v_lower[rr] * 0x00010001u;
     } else {
-#pragma unroll
-      for (int u = 0; u < 8; ++u) xv[u] = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-      for (int q = 0; q < 16; ++q) tv[q] = 0u;
+      if (!page_lock(rec + 3, err)) continue;
+      rc = __ldcg(reinterpret_cast<const uint4*>(rec));
+      if (!IS_V) {
+        smin = __ldcg(reinterpret_cast<const uint2*>(st));
+        smax = __ldcg(reinterpret_cast<const uint2*>(st + PF_D));
+      }
     }
-    const uint32_t vx = tv[15];
-    uint32_t vw[8];  // nuq4: 8 words (32 B); nuq2: words 0..3 (16 B)
+    ListRec LR = {rc.x, rc.y, rc.z, rc.w & kRowsMask};
+    if ((int)LR.rows > t0) LR.cnt = list_filter(pool.arena, LR, t0, t0 + n);  // an overwrite
+    bool ok;
     {
-      uint64_t vslow = 0;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint32_t xx[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
-        uint32_t w = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t c = codes2<BV>(xx[k], tv);
-          if (BV == 4) w |= ((c & 0xFu) | ((c >> 12) & 0xF0u)) << (8 * k);
-          else w |= ((c & 3u) | ((c >> 14) & 0xCu)) << (4 * k);
-          const uint32_t o = gt2(xx[k], vup) | lt2(xx[k], vlo);
-          const uint32_t sl = geu2(xx[k], vx);
-          voutm |= (uint64_t)((o & 1u) | ((o >> 15) & 2u)) << (8 * u + 2 * k);
-          vslow |= (uint64_t)((sl & 1u) | ((sl >> 15) & 2u)) << (8 * u + 2 * k);
-        }
-        if (BV == 4) vw[u] = w;
-        else if (u & 1) vw[u >> 1] |= w << 16;
-        else vw[u >> 1] = w;
-      }
-      if (!vact) voutm = vslow = 0;
-      if (__any_sync(0xffffffffu, vslow != 0)) {
-        // elements outside the fast range: the reference's scan, patched into the words
-        const uint16_t* prow = sc.v_poles + ((int64_t)h * Tc + vrow) * LV;
-        uint64_t m = vslow;
-        while (m) {
-          const int b = __ffsll((long long)m) - 1;  // channel 8u + 2k + e of the half row
-          m &= m - 1;
-          float pole;
-          const int c = scan_code(h2f(value[((int64_t)iv * H + h) * PF_D + 64 * hf + b]), prow, LV, pole);
-          if (BV == 4) {
-            const int wi = b >> 3, sh = 4 * (b & 7);
-            vw_set(vw, wi, sh, 0xFu, (uint32_t)c);
-          } else {
-            const int wi = b >> 4, sh = 2 * (b & 15);
-            vw_set(vw, wi, sh, 0x3u, (uint32_t)c);
-          }
-        }
-      }
+      ListRec none = {0u, 0u, 0u, 0u};
+      bool ok2;
+      lists_reserve(pool, LR, LR.cnt + tot, none, 0u, ok, ok2, err);
     }
-    if (vact) {
-      uint4* dst = reinterpret_cast<uint4*>(seg + PF_S * RBK + t * RBV + hf * (RBV / 2));
-      dst[0] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
-      if (BV == 4) dst[1] = make_uint4(vw[4], vw[5], vw[6], vw[7]);
-    }
-
-    // V entries (lane-major = slot, then channel), staged after K's
-    int totv;
-    const int basev = warp_excl_scan(__popcll(voutm), totv);
-    {
-      uint64_t m = voutm;
-      int q = totk + basev;
-      while (m) {
-        const int b = __ffsll((long long)m) - 1;
-        m &= m - 1;
-        if (q < PF_STAGE) sent[q] = (uint32_t)vval(xv, b) | ((uint32_t)(64 * hf + b) << 16) | ((uint32_t)t << 24);
-        ++q;
-      }
-    }
-
-    // ---- page lists and stats
-    if (!excl) {
-      if (!page_lock(dk + 3, err)) continue;
-      rk = __ldcg(reinterpret_cast<const uint4*>(dk));
-      rv = __ldcg(reinterpret_cast<const uint4*>(dv));
-      smin = __ldcg(reinterpret_cast<const uint2*>(st));
-      smax = __ldcg(reinterpret_cast<const uint2*>(st + PF_D));
-    }
-    ListRec LKr = {rk.x, rk.y, rk.z, rk.w & ~kPageLock}, LVr = {rv.x, rv.y, rv.z, 0u};
-    if ((int)LKr.rows > t0) {  // an overwrite: drop the old entries of these slots
-      LKr.cnt = list_filter(pool.arena, LKr, t0, t0 + n);
-      LVr.cnt = list_filter(pool.arena, LVr, t0, t0 + n);
-    }
-    bool okk, okv;
-    lists_reserve(pool, LKr, LKr.cnt + totk, LVr, LVr.cnt + totv, okk, okv, err);
     __syncwarp();
-    {
-      // staged entries, coalesced
-      const int ns = min(totk + totv, PF_STAGE);
-      uint32_t* dk_e = pool.arena + LKr.off + LKr.cnt;
-      uint32_t* dv_e = pool.arena + LVr.off + LVr.cnt - totk;
-      for (int q = lane; q < ns; q += 32) {
-        const uint32_t e = sent[q];
-        if (q < totk) {
-          if (okk) dk_e[q] = e;
-        } else if (okv) {
-          dv_e[q] = e;
-        }
-      }
-      if (totk + totv > PF_STAGE) {  // entries past the staging buffer: rebuilt from the inputs
-#pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-          uint32_t m = hb ? kout1 : kout0;
-          int q = hb ? kbase1 : kbase0;
-          while (m) {
-            const int b = __ffs(m) - 1;
-            m &= m - 1;
-            if (q >= PF_STAGE && okk) {
-              const int j = 8 * hb + (b >> 2), c = 4 * lane + (b & 3);
-              dk_e[q] = (uint32_t)key[((int64_t)(i + j) * H + h) * PF_D + c] | ((uint32_t)c << 16) |
-                        ((uint32_t)(t0 + j) << 24);
-            }
-            ++q;
-          }
-        }
-        uint64_t m = voutm;
-        int q = totk + basev;
-        while (m) {
-          const int b = __ffsll((long long)m) - 1;
-          m &= m - 1;
-          if (q >= PF_STAGE && okv) {
-            const int c = 64 * hf + b;
-            dv_e[q] = (uint32_t)value[((int64_t)iv * H + h) * PF_D + c] | ((uint32_t)c << 16) | ((uint32_t)t << 24);
-          }
-          ++q;
-        }
-      }
-      if (okk) LKr.cnt += totk;
-      if (okv) LVr.cnt += totv;
+    if (ok) {
+      uint32_t* de = pool.arena + LR.off + LR.cnt;
+      for (int q = lane; q < tot; q += 32) de[q] = sent[q];
+      LR.cnt += tot;
     }
-    // K page stats: the run's reconstructed min / max folded into the page's
-    {
+    if (!IS_V) {  // K page stats: the run's reconstructed min / max folded into the page's
       uint32_t nmin[2], nmax[2];
-      const uint16_t* kp = sc.k_poles + ((int64_t)h * PF_D + 4 * lane) * LK;
+      const uint16_t* kp = sc.k_poles + ((int64_t)h * PF_D + 4 * lane) * L;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint32_t cm = k < 2 ? cmina : cminb, cx = k < 2 ? cmaxa : cmaxb;
         const int lo = half_of(cm, k & 1), hi1 = half_of(cx, k & 1);
         float mn = emin[k], mx = emax[k];
-        if (lo < 16) mn = fminf(mn, h2f(kp[k * LK + lo]));
-        if (hi1 > 0) mx = fmaxf(mx, h2f(kp[k * LK + hi1 - 1]));
+        if (lo < 16) mn = fminf(mn, h2f(kp[k * L + lo]));
+        if (hi1 > 0) mx = fmaxf(mx, h2f(kp[k * L + hi1 - 1]));
         const float om = h2f(half_of(k < 2 ? smin.x : smin.y, k & 1));
         const float oM = h2f(half_of(k < 2 ? smax.x : smax.y, k & 1));
         const uint16_t rm = mn < om ? f2h(mn) : f2h(om);
@@ -665,21 +685,20 @@ __global__ void __launch_bounds__(128, 4)
       *reinterpret_cast<uint2*>(st) = make_uint2(nmin[0], nmin[1]);
       *reinterpret_cast<uint2*>(st + PF_D) = make_uint2(nmax[0], nmax[1]);
     }
-    const uint32_t rows_new = max(LKr.rows, (uint32_t)(t0 + n));
+    const uint32_t rows_new = max(LR.rows, (uint32_t)(t0 + n));
     if (excl) {
-      if (lane == 0) {
-        *reinterpret_cast<uint4*>(dk) = make_uint4(LKr.off, LKr.cap, LKr.cnt, rows_new);
-        *reinterpret_cast<uint4*>(dv) = make_uint4(LVr.off, LVr.cap, LVr.cnt, 0u);  // run count back to 0
-      }
+      if (lane == 0) *reinterpret_cast<uint4*>(rec) = make_uint4(LR.off, LR.cap, LR.cnt, rows_new);  // runs, lock 0
     } else {
       __threadfence();  // this warp's entries and stats are visible before the page is released
       __syncwarp();
       if (lane == 0) {
-        dk[0] = LKr.off; dk[1] = LKr.cap; dk[2] = LKr.cnt;
-        dv[0] = LVr.off; dv[1] = LVr.cap; dv[2] = LVr.cnt;
-        atomicSub(dv + 3, 1u);  // one run of this page done
+        rec[0] = LR.off;
+        rec[1] = LR.cap;
+        rec[2] = LR.cnt;
+        const uint32_t w = __ldcg(rec + 3);
+        const uint32_t runs = (w & kRunsMask) ? (w & kRunsMask) - kRunsOne : 0u;
         __threadfence();
-        atomicExch(dk + 3, rows_new);  // rows, lock bit clear
+        atomicExch(rec + 3, rows_new | runs);  // one run of this page done, lock clear
       }
     }
     __syncwarp();
@@ -687,8 +706,9 @@ __global__ void __launch_bounds__(128, 4)
 }
 
 // Pre-pass of hx_pack_append's bandwidth path: count the runs each (head,
-// page) receives in this launch into the last word of the page's V record
-// (the pack kernel resets it). Same run rule as pack_fast_kernel.
+// page) receives in this launch into its K and V records (bits 8-30 of the
+// last word; the pack kernels take them out again). Same run rule as the
+// pack kernels.
 __global__ void pack_count_runs_kernel(const hx_pool_layer pool, const int64_t* __restrict__ slots, int T) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int H = pool.num_kv_heads;
@@ -702,7 +722,9 @@ __global__ void pack_count_runs_kernel(const hx_pool_layer pool, const int64_t* 
   }
   const int64_t pg = s / PF_S;
   if (pg >= pool.num_blocks) return;
-  atomicAdd(pool.dir + (((int64_t)h * pool.num_blocks + pg) * 2 + 1) * 4 + 3, 1u);
+  uint32_t* rec = pool.dir + ((int64_t)h * pool.num_blocks + pg) * 8;
+  atomicAdd(rec + 3, kRunsOne);
+  atomicAdd(rec + 7, kRunsOne);
 }
 
 }  // namespace hx
@@ -726,27 +748,33 @@ int hx_pack_fast_launch(cudaStream_t s, const hx_pool_layer* pool, const hx_laye
   if (blocks > 0x7fffffff || (cthreads + 255) / 256 > 0x7fffffff) return HX_ERR_ARG;
   pack_count_runs_kernel<<<(unsigned)((cthreads + 255) / 256), 256, 0, s>>>(*pool, slots, T);
   const dim3 grid((unsigned)blocks), block(128);
-#define HX_PF(BK_, BV_) pack_fast_kernel<BK_, BV_><<<grid, block, 0, s>>>(*pool, *sc, key, value, slots, abspos, T, dev_err)
-  if (pool->bits_k == 4 && pool->bits_v == 4) HX_PF(4, 4);
-  else if (pool->bits_k == 4) HX_PF(4, 2);
-  else if (pool->bits_v == 4) HX_PF(2, 4);
-  else HX_PF(2, 2);
-#undef HX_PF
+  if (pool->bits_k == 4) pack_list_kernel<4, false><<<grid, block, 0, s>>>(*pool, *sc, key, slots, abspos, T, dev_err);
+  else pack_list_kernel<2, false><<<grid, block, 0, s>>>(*pool, *sc, key, slots, abspos, T, dev_err);
+  if (pool->bits_v == 4) pack_list_kernel<4, true><<<grid, block, 0, s>>>(*pool, *sc, value, slots, abspos, T, dev_err);
+  else pack_list_kernel<2, true><<<grid, block, 0, s>>>(*pool, *sc, value, slots, abspos, T, dev_err);
   HX_LAUNCH_CHECK();
   return HX_OK;
 }
 
 extern "C" {
 
-HX_API int hx_scales_prepare(void* stream, const hx_layer_scales* sc, int32_t H, int32_t D, uint32_t* k_thresh,
-                             uint32_t* v_thresh) {
+HX_API int hx_scales_prepare(void* stream, const hx_layer_scales* sc, int32_t H, int32_t D, int32_t bits_k,
+                             int32_t bits_v, uint32_t* k_thresh, uint32_t* v_thresh, uint32_t* dec_tabs) {
   if (!sc || !sc->k_poles || !sc->v_poles || H <= 0 || D <= 0 || (D & 1) || !k_thresh || !v_thresh) return HX_ERR_ARG;
   if (sc->levels_k < 1 || sc->levels_k > 16 || sc->levels_v < 1 || sc->levels_v > 16 || sc->t_cal < 1)
+    return HX_ERR_ARG;
+  if ((bits_k != 2 && bits_k != 4) || (bits_v != 2 && bits_v != 4) || sc->levels_k > (1 << bits_k) ||
+      sc->levels_v > (1 << bits_v))
     return HX_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int64_t rk = (int64_t)H * D, rv = (int64_t)H * sc->t_cal;
   scales_prepare_kernel<<<(unsigned)((rk + 127) / 128), 128, 0, s>>>(0, sc->k_poles, rk, sc->levels_k, k_thresh);
   scales_prepare_kernel<<<(unsigned)((rv + 127) / 128), 128, 0, s>>>(1, sc->v_poles, rv, sc->levels_v, v_thresh);
+  if (dec_tabs) {
+    if (D != 128) return HX_ERR_UNSUPPORTED;
+    const int64_t nw = (int64_t)H * kDecTabWords;
+    decode_tables_kernel<<<(unsigned)((nw + 255) / 256), 256, 0, s>>>(*sc, H, bits_k, bits_v, dec_tabs);
+  }
   HX_LAUNCH_CHECK();
   return HX_OK;
 }

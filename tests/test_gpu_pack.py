@@ -201,9 +201,9 @@ def test_pool_slots_in_any_order(layout):
         np.testing.assert_array_equal(a, b)
     np.testing.assert_array_equal(np16(gpu.layers[0].stats).view(np.uint16), orc.stats[0].view(np.uint16))
     assert gpu_outlier_sets(gpu, 0) == oracle_outlier_sets(orc, 0)
+    # a record's last word: rows (bits 0-7) | this launch's run count (8-30) | lock (31)
     last = np16(gpu.layers[0].dir)[..., 3].view(np.uint32)      # (H, NB, 2)
-    assert (last[..., 0] & 0x80000000 == 0).all()                # every page lock released
-    assert (last[..., 1] == 0).all()                             # every per-launch run count back to 0
+    assert (last & np.uint32(0xFFFFFF00) == 0).all()             # run counts back to 0, locks released
 
 
 def test_pool_incremental_appends_and_overwrite():
