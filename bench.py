@@ -332,7 +332,6 @@ def check_parity(W, args, world, rank, group):
     from kvquant import fused
     from oracle import attention as oatt
     from oracle import quest as oq
-    from oracle.packing import rows_from_segment
     from oracle.pool import dequant_packed_pages
 
     pool, shard, qs, bt, sl = W["pool"], W["shard"], W["qs"], W["bt"], W["sl"]
@@ -365,8 +364,8 @@ def check_parity(W, args, world, rank, group):
             pages = oq.select_pages(ref_scores[:, h], W["k"], shard.sink_pages)
             c = int(counts[0, h])
             sel_ok &= bool(np.array_equal(lists[0, h, :c].cpu().numpy(), pages))
-            kr = rows_from_segment(codes[h, :, :S * rbk], S)
-            vr = rows_from_segment(codes[h, :, S * rbk:], S)
+            kr = codes[h, :, :S * rbk].reshape(n, S, rbk)
+            vr = codes[h, :, S * rbk:].reshape(n, S, rbv)
             Kd, Vd = dequant_packed_pages(kr, vr, dirs[h], arena, pages, (shard.page_begin + pages) * S,
                                           kpol[h], vpol[h], lay.bits_k, lay.bits_v)
             Kt = np.zeros((Kd.shape[0] * S, H, D), np.float16)

@@ -8,17 +8,13 @@
 // src/quest/reference.py:136-168 (softmax(q.K^T * scale) V, fp32 softmax),
 // generalised to grouped-query heads (query head h*G+g reads KV head h).
 //
-// One CTA = (split, KV head, sequence), 10 warps, one CTA per SM; the CTA's
-// pages (a balanced share of the selected list) are dealt to the warps. The
-// head's level tables (96 KB, built once by hx_scales_prepare) come in by one
-// bulk copy. Each warp streams its pages: bulk copies (cp.async.bulk, no
-// multicast) of the page's code segment, its outlier entries and, before
-// t_cal, its per-token V level rows into a 2-stage buffer; table dequant of
-// the 16 x 128 K tile into swizzled smem (lane l owns byte columns l and
-// l + 32, each a channel pair, or column l, a channel quad, of the page's
-// column-major code block, and looks a byte up in its own bank column of the
-// tables: one 4- or 8-byte load for 2 or 4 channels, conflict-free), outlier
-// patch, ldmatrix + mma.sync (tokens x heads), online softmax in fp32 (exp2 domain;
+// One CTA = (split, KV head, sequence), 16 warps, one CTA per SM; the CTA's
+// pages (a balanced share of the selected list) are dealt to the warps. Each
+// warp streams its pages: bulk copies (cp.async.bulk, no multicast) of the
+// page's code segment, its outlier entries and, before t_cal, its per-token V
+// level rows into a 2-stage buffer; LUT dequant of the 16 x 128 K tile into
+// swizzled smem (one prmt-built table address per code), outlier patch,
+// ldmatrix + mma.sync (tokens x heads), online softmax in fp32 (exp2 domain;
 // the running max moves only when a score passes it by 2^8), P split into
 // fp16 hi + lo parts so P.V keeps ~22 bits, V tile the same way, PV with two
 // MMAs per m-tile. Warps merge in smem; the last CTA of each (b, h) merges
@@ -31,13 +27,11 @@ namespace hx {
 
 constexpr int DD = 128;          // head_size
 constexpr int DS = 16;           // page size (tokens)
-constexpr int NW = 10;           // warps per CTA (one CTA per SM; the level tables take 96 KB)
+constexpr int NW = 16;           // warps per CTA (one CTA per SM, 128 registers a thread)
 constexpr int NT = NW * 32;
 constexpr int NSTAGE = 2;        // pages in smem per warp (one in flight while one is used)
-constexpr int LISTCAP = 256;     // pages gathered per round
-constexpr int ENTCAP = 256;      // outlier entries staged per page, K's then V's (the rest read from the arena)
-constexpr int KTABW = 16384;     // K level tables: 256 rows (code byte) x 64 words
-constexpr int VTABW = 8192;      // V levels beyond t_cal: 256 rows x 32 words (replicated)
+constexpr int LISTCAP = 512;     // pages gathered per round
+constexpr int ENTCAP = 352;      // outlier entries staged per page, K's then V's (nuq2 pages: ~100 + ~150)
 constexpr int SEGMAX = DS * DD;  // codes bytes per page segment at 4+4 bits
 constexpr int PSZ = 8 * DD + 16; // floats per split partial: O[8][128], m[8], l[8]
 constexpr int MAXSPLIT = 1024;   // splits the final merge stages weights for
@@ -78,10 +72,10 @@ struct __align__(256) WarpSmem {
 };
 
 struct __align__(256) CtaSmem {
-  uint32_t ktab[KTABW];                 // the head's K tables (hx_scales_prepare's dec_tabs layout)
-  uint32_t vtab[VTABW];                 // its V tables beyond t_cal
   WarpSmem w[NW];
-  uint64_t tbar;                        // completes the tables' bulk copy
+  alignas(256) uint16_t klut[16 * DD + 64];  // K tables (bank-spread, 256-aligned; layout at the fill)
+  alignas(256) uint16_t vtail[16];           // V levels at positions >= t_cal (256-aligned)
+  alignas(256) uint32_t vpair[16];           // nuq2: the same as level pairs (entry c0 | c1 << 2)
   int32_t pages[LISTCAP];
   int32_t phys[LISTCAP];
   uint4 dir[LISTCAP][2];                // K and V directory records of each page
@@ -92,10 +86,10 @@ struct __align__(256) CtaSmem {
   int32_t slice0, slice0_off;           // HX_SEL_SLICES: slice holding the CTA's first rank, its offset
 };
 
-static_assert(sizeof(CtaSmem) <= 232448, "the decode's shared memory exceeds 227 KB");
-static_assert(sizeof(WarpSmem) * NW >= 3 * MAXSPLIT * 8 * sizeof(float), "merge staging does not fit the warp buffers");
-
-// shared-memory helpers of the table dequant
+// LUT dequant helpers. A table of 2-byte levels sits 256-aligned in smem; the
+// element's byte (2 * code, with the lane's table-offset low bits OR-ed in)
+// replaces the low byte of the table's base address in one prmt, and the
+// load carries the per-channel offset as its immediate.
 HX_DEVINL uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
@@ -105,6 +99,24 @@ HX_DEVINL uint16_t lds16(uint32_t addr) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
+}
+
+// 8 levels for 8 consecutive 4-bit codes of word w (channels c0 .. c0+7):
+// tab(c) = base + off + TSTRIDE * (c - c0). Only base's low byte is replaced,
+// so off (a multiple of the table span, folded into the load's immediate once
+// unrolled) must be added after the prmt.
+template <int TSTRIDE>
+HX_DEVINL uint4 lut8_nib(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t off) {
+  const uint32_t lo = ((w << 1) & 0x1E1E1E1Eu) | lowbits;  // 2 * code of nibbles 0, 2, 4, 6
+  const uint32_t hi = ((w >> 3) & 0x1E1E1E1Eu) | lowbits;  // nibbles 1, 3, 5, 7
+  uint16_t v[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[2 * k] = lds16(prmt(lo, base, 0x7650u | k) + off + TSTRIDE * (2 * k));
+    v[2 * k + 1] = lds16(prmt(hi, base, 0x7650u | k) + off + TSTRIDE * (2 * k + 1));
+  }
+  return make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
+                    pack_u16x2(v[6], v[7]));
 }
 
 HX_DEVINL void sts128(uint32_t addr, const uint4& v) {
@@ -126,19 +138,43 @@ HX_DEVINL uint32_t lds32(uint32_t addr) {
   return v;
 }
 
-HX_DEVINL uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
+// 16 levels for 16 consecutive 2-bit codes of word w from level-pair tables:
+// a nibble (two codes) picks one 4-byte entry holding both levels, so each
+// load yields two channels. tab(pair n) = base + off + TSTRIDE * n, entry
+// 4 * nibble; as in lut8_nib only base's low byte is replaced.
+template <int TSTRIDE>
+HX_DEVINL void lut8_pair(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t off, uint4& o0, uint4& o1) {
+  const uint32_t lo = ((w << 2) & 0x3C3C3C3Cu) | lowbits;  // 4 * low nibble: codes 4k, 4k+1
+  const uint32_t hi = ((w >> 2) & 0x3C3C3C3Cu) | lowbits;  // 4 * high nibble: codes 4k+2, 4k+3
+  uint32_t v[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[2 * k] = lds32(prmt(lo, base, 0x7650u | k) + off + TSTRIDE * (2 * k));
+    v[2 * k + 1] = lds32(prmt(hi, base, 0x7650u | k) + off + TSTRIDE * (2 * k + 1));
+  }
+  o0 = make_uint4(v[0], v[1], v[2], v[3]);
+  o1 = make_uint4(v[4], v[5], v[6], v[7]);
 }
-HX_DEVINL void sts32(uint32_t addr, uint32_t v) { asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v)); }
-HX_DEVINL void sts64(uint32_t addr, uint2 v) {
-  asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(v.x), "r"(v.y));
+
+// 16 levels for 16 consecutive 2-bit codes of word w, as two 8-wide chunks.
+template <int TSTRIDE>
+HX_DEVINL void lut16_crumb(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t off, uint4& o0,
+                           uint4& o1) {
+  uint32_t g[4];
+  g[0] = ((w << 1) & 0x06060606u) | lowbits;  // crumbs 0, 4, 8, 12
+  g[1] = ((w >> 1) & 0x06060606u) | lowbits;  // crumbs 1, 5, 9, 13
+  g[2] = ((w >> 3) & 0x06060606u) | lowbits;  // crumbs 2, 6, 10, 14
+  g[3] = ((w >> 5) & 0x06060606u) | lowbits;  // crumbs 3, 7, 11, 15
+  uint16_t v[16];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int sft = 0; sft < 4; ++sft)
+      v[4 * k + sft] = lds16(prmt(g[sft], base, 0x7650u | k) + off + TSTRIDE * (4 * k + sft));
+  o0 = make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]), pack_u16x2(v[6], v[7]));
+  o1 = make_uint4(pack_u16x2(v[8], v[9]), pack_u16x2(v[10], v[11]), pack_u16x2(v[12], v[13]),
+                  pack_u16x2(v[14], v[15]));
 }
-// byte k of w shifted to bit 8 (a 256-byte table row offset)
-HX_DEVINL uint32_t byte_row256(uint32_t w, int k) { return prmt(w, 0u, 0x4404u | ((uint32_t)k << 4)); }
-// byte k of w as a 128-byte table row offset
-HX_DEVINL uint32_t byte_row128(uint32_t w, int k) { return prmt(w, 0u, 0x4440u | (uint32_t)k) << 7; }
 
 // Tile layout: 16 tokens x 128 channels fp16, 256 bytes a token; 16-byte chunk
 // c (channels 8c .. 8c+7) of token t sits at position c ^ (t & 7) ^ 4 (c >> 3)
@@ -198,17 +234,46 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   const int NB = p.pool.num_blocks;
   pdl_allow_next();
 
-  // ---- the head's level tables (calibration data, built by hx_scales_prepare
-  // in this layout): one bulk copy of 96 KB while the previous kernel finishes
-  if (tid == 0) {
-    mbar_init(&sm.tbar, 1);
-    fence_mbar_init();
-    const uint32_t* src = p.sc.dec_tabs + (int64_t)h * (KTABW + VTABW);
-    fence_proxy_async();
-    mbar_arrive_expect_tx(&sm.tbar, 4u * (KTABW + VTABW));
-    bulk_g2s(sm.ktab, src, 4u * KTABW, &sm.tbar);
-    bulk_g2s(sm.vtab, src + KTABW, 4u * VTABW, &sm.tbar);
+  // ---- per-CTA tables (all of a thread's loads in flight before its stores).
+  // nuq4 K: channel d's 16 levels (32 B) at byte 32 d + 32 (d >> 5). nuq2 K:
+  // channel pair P = (2P, 2P+1) as 16 level pairs (64 B; entry e holds the
+  // levels of codes e & 3 and e >> 2) at byte 64 P + 64 (P >> 5). Either way the
+  // tables a dequant load touches at once sit in disjoint bank windows.
+  auto kpole = [&](int d, int c) -> uint16_t {
+    return c < p.sc.levels_k ? p.sc.k_poles[((int64_t)h * DD + d) * p.sc.levels_k + c] : (uint16_t)0;
+  };
+  auto vtail_level = [&](int c) -> uint16_t {
+    return c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + (Tc - 1)) * p.sc.levels_v + c] : (uint16_t)0;
+  };
+  if (BK == 4) {
+    constexpr int PER = (16 * DD + NT - 1) / NT;
+    uint16_t kv[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT;
+      kv[u] = i < 16 * DD ? kpole(i >> 4, i & 15) : (uint16_t)0;
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT, d = i >> 4;
+      if (i < 16 * DD) sm.klut[16 * d + 16 * (d >> 5) + (i & 15)] = kv[u];
+    }
+  } else {
+    constexpr int PER = (16 * (DD / 2) + NT - 1) / NT;
+    uint32_t kv[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT, P = i >> 4, e = i & 15;
+      kv[u] = i < 16 * (DD / 2) ? pack_u16x2(kpole(2 * P, e & 3), kpole(2 * P + 1, e >> 2)) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = tid + u * NT, P = i >> 4;
+      if (i < 16 * (DD / 2)) reinterpret_cast<uint32_t*>(sm.klut)[16 * P + 16 * (P >> 5) + (i & 15)] = kv[u];
+    }
   }
+  if (tid < NLV) sm.vtail[tid] = vtail_level(tid);
+  if (BV == 2 && tid >= 32 && tid < 48) sm.vpair[tid - 32] = pack_u16x2(vtail_level((tid - 32) & 3), vtail_level((tid - 32) >> 2));
   WarpSmem& ws = sm.w[warp];
   if (lane == 0) {
     for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
@@ -217,13 +282,6 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   // everything above reads calibration tables only; from here on the inputs
   // may come from the kernels before this one
   pdl_wait();
-  __syncthreads();  // the table barrier is initialised
-  if (!__syncthreads_and(mbar_wait(&sm.tbar, 0))) {
-    // the tables did not arrive: one more bounded wait for the copy, flag, leave
-    (void)mbar_wait(&sm.tbar, 0);
-    if (tid == 0) set_err(p.err, HX_DEV_ERR_TIMEOUT);
-    return;
-  }
   const int seq_len = p.seq_lens[b];
   const int n = min((seq_len + DS - 1) / DS, p.max_pages);
   // HX_SEL_SLICES: the row's slice offsets (exclusive selected counts of the
@@ -234,17 +292,16 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   const int32_t soff_lo = (slices && tid < nsl) ? soff[tid] : 0, soff_hi = (slices && tid < nsl) ? soff[tid + 1] : 0;
   const int32_t soff_all = slices ? soff[nsl] : 0;
 
-  // Dequant lanes: lane l owns byte columns l and l + 32 of a 64-column block
-  // (nuq4: channel pairs l, l + 32) or column l of a 32-column block (nuq2:
-  // channel quad l), over the page's 16 slots; its tables sit in bank column l.
-  // Tile: 16 tokens x 128 channels fp16, token t's 16-byte chunk c at
-  // tile + 256 t + 16 (c ^ (t & 7) ^ 4 (c >> 3)). Lane bases for the dequant
-  // stores (the t-dependent XOR and 256 t are applied per token):
+  // dequant lanes: token t = lane >> 1, row half = lane & 1; x0 = which
+  // 16-byte chunk of its half row (nuq4) the lane reads first is cx0
+  const int t = lane >> 1, half = lane & 1, cx0 = (lane >> 2) & 1;
+  // Tile byte addresses (the tile is 256-aligned): chunk c of token t is at
+  // tile + 256 t + 16 (c ^ (t & 7) ^ 4 (c >> 3)). With c = 8 half + low, a
+  // lane's dequant store is tw ^ 16 low, and each ldmatrix phase reads a lane
+  // base ^ 16 k(step) with k(s) = 2 s ^ 4 (s >> 2).
   const uint32_t tile0 = smem_u32(ws.tile);
-  const uint32_t tl4 = tile0 + 16u * (lane >> 2) + 4u * (lane & 3);                      // nuq4: pair l
-  const uint32_t tl2 = (tile0 + 16u * (lane >> 1) + 8u * (lane & 1)) ^ (lane >= 16 ? 64u : 0u);  // nuq2: quad l
-  const uint32_t ktab_l = smem_u32(sm.ktab) + (BK == 4 ? 4u : 8u) * lane;
-  const uint32_t vtab_l = smem_u32(sm.vtab) + (BV == 4 ? 4u * lane : 8u * (lane & 15));
+  const uint32_t tw = tile0 + 256u * t + 16u * ((8 * half) ^ (4 * half) ^ (t & 7));
+  const uint32_t tw4 = tw ^ (64u * cx0);  // nuq4: chunk order cx0, cx0 ^ 1
   uint32_t tqk, tpv;
   {
     const int rk = (lane & 7) + ((lane >> 3) & 1) * 8, rv = (lane & 7) + ((lane >> 4) & 1) * 8;
@@ -466,25 +523,38 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       const int pos0 = vpos0(li);
       const int valid = seq_len - j * DS;  // tokens of this page inside the sequence
 
-      // ---- K tile: lane l looks its byte columns up in its bank column of the
-      // K tables (one 4- or 8-byte load gives 2 or 4 channels of a token)
-      if (BK == 4) {
-        const uint4 ca = *reinterpret_cast<const uint4*>(ws.raw[st] + 16 * lane);         // pair l
-        const uint4 cb = *reinterpret_cast<const uint4*>(ws.raw[st] + 16 * (lane + 32));  // pair l + 32
-        const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w}, wb[4] = {cb.x, cb.y, cb.z, cb.w};
+      // ---- K tile: per-channel tables (lane = token t, half of the channels)
+      {
+        const uint8_t* rowp = ws.raw[st] + t * RBK + half * (RBK / 2);
+        if (BK == 4) {
+          // the half row's two 16-byte chunks in the lane's order cx0, cx0 ^ 1, so
+          // the 8 lanes of a wavefront read 8 distinct bank groups
+          const uint4 ca = *reinterpret_cast<const uint4*>(rowp + 16 * cx0);
+          const uint4 cb = *reinterpret_cast<const uint4*>(rowp + 16 * (cx0 ^ 1));
+          const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
-        for (int tt = 0; tt < DS; ++tt) {
-          const uint32_t va = lds32(ktab_l + byte_row256(wa[tt >> 2], tt & 3));
-          const uint32_t vb = lds32(ktab_l + 128u + byte_row256(wb[tt >> 2], tt & 3));
-          sts32((tl4 ^ (16u * (tt & 7))) + 256u * tt, va);
-          sts32((tl4 ^ (16u * ((tt & 7) ^ 4))) + 128u + 256u * tt, vb);
+          for (int j = 0; j < 2; ++j) {
+            // channels 64 half + 32 x .. +31: tables at klut + 2048 half + 1024 x
+            // + 64 half + 32 x (+ 256 per 8 channels); the last term is the low byte
+            const int x = cx0 ^ j;
+            const uint32_t base = smem_u32(sm.klut) + 2048u * half + 1024u * x;
+            const uint32_t low = (64u * half + 32u * x) * 0x01010101u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sts128(tw4 ^ (64u * j + 16u * i), lut8_nib<32>(wv[4 * j + i], low, base, 256u * i));
+          }
+        } else {
+          // pair P = 32 half + 8 w + n at klut + 2048 half + 64 half + 512 w + 64 n
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+          const uint32_t base = smem_u32(sm.klut) + 2048u * half, low = 64u * half * 0x01010101u;
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            uint4 o0, o1;
+            lut8_pair<64>(wv[w4], low, base, 512u * (uint32_t)w4, o0, o1);
+            sts128(tw ^ (32u * w4), o0);
+            sts128(tw ^ (32u * w4 + 16u), o1);
+          }
         }
-      } else {
-        const uint4 ca = *reinterpret_cast<const uint4*>(ws.raw[st] + 16 * lane);         // quad l
-        const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
-#pragma unroll
-        for (int tt = 0; tt < DS; ++tt)
-          sts64((tl2 ^ (16u * (tt & 7))) + 256u * tt, lds64(ktab_l + byte_row256(wa[tt >> 2], tt & 3)));
       }
       __syncwarp();
       const uint32_t ek = stage_k(cntk);  // K entries staged; V's follow them
@@ -543,71 +613,61 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       const uint32_t bh0 = movmatrix_trans(phi_top), bh1 = movmatrix_trans(phi_bot);
       const uint32_t bl0 = movmatrix_trans(plo_top), bl1 = movmatrix_trans(plo_bot);
 
-      // ---- V tile: beyond t_cal every token has the same levels (the lane's
-      // copy of the V tables); before it each token its own row, row min(pos,
-      // t_cal - 1), staged with the page or gathered here
-      {
-        const uint8_t* vc = ws.raw[st] + DS * RBK;
-        if (pos0 >= Tc) {
-          if (BV == 4) {
-            const uint4 ca = *reinterpret_cast<const uint4*>(vc + 16 * lane);
-            const uint4 cb = *reinterpret_cast<const uint4*>(vc + 16 * (lane + 32));
-            const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w}, wb[4] = {cb.x, cb.y, cb.z, cb.w};
-#pragma unroll
-            for (int tt = 0; tt < DS; ++tt) {
-              const uint32_t va = lds32(vtab_l + byte_row128(wa[tt >> 2], tt & 3));
-              const uint32_t vb = lds32(vtab_l + byte_row128(wb[tt >> 2], tt & 3));
-              sts32((tl4 ^ (16u * (tt & 7))) + 256u * tt, va);
-              sts32((tl4 ^ (16u * ((tt & 7) ^ 4))) + 128u + 256u * tt, vb);
-            }
-          } else {
-            const uint4 ca = *reinterpret_cast<const uint4*>(vc + 16 * lane);
-            const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
-#pragma unroll
-            for (int tt = 0; tt < DS; ++tt)
-              sts64((tl2 ^ (16u * (tt & 7))) + 256u * tt, lds64(vtab_l + byte_row128(wa[tt >> 2], tt & 3)));
-          }
+      // ---- V tile: per-token LUT (row min(pos, t_cal - 1))
+      const bool vshared = pos0 >= Tc;
+      uint32_t vbase, vlow;
+      if (vshared) {
+        vbase = smem_u32(sm.vtail);  // one table for every token
+        vlow = 0u;
+      } else {
+        if (v_bulk(pos0)) {
+          vbase = smem_u32(ws.vp[st]);
         } else {
-          uint32_t vrow;  // smem address of token 0's NLV levels (rows of 2 NLV bytes)
-          if (v_bulk(pos0)) {
-            vrow = smem_u32(ws.vp[st]);
-          } else {
-            uint16_t lv[DS * NLV / 32];
+          uint16_t lv[DS * NLV / 32];
 #pragma unroll
-            for (int u = 0; u < DS * NLV / 32; ++u) {
-              const int i = lane + 32 * u;
-              const int r = i / NLV, c = i % NLV;
-              const int pr = min(pos0 + r, Tc - 1);
-              lv[u] = c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + pr) * p.sc.levels_v + c] : (uint16_t)0;
-            }
-#pragma unroll
-            for (int u = 0; u < DS * NLV / 32; ++u) ws.vlut[lane + 32 * u] = lv[u];
-            __syncwarp();
-            vrow = smem_u32(ws.vlut);
+          for (int u = 0; u < DS * NLV / 32; ++u) {
+            const int i = lane + 32 * u;
+            const int r = i / NLV, c = i % NLV;
+            const int pr = min(pos0 + r, Tc - 1);
+            lv[u] = c < p.sc.levels_v ? p.sc.v_poles[((int64_t)h * Tc + pr) * p.sc.levels_v + c] : (uint16_t)0;
           }
-          if (BV == 4) {
-            const uint4 ca = *reinterpret_cast<const uint4*>(vc + 16 * lane);
-            const uint4 cb = *reinterpret_cast<const uint4*>(vc + 16 * (lane + 32));
-            const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w}, wb[4] = {cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
-            for (int tt = 0; tt < DS; ++tt) {
-              const uint32_t rw = vrow + 32u * tt;
-              const uint32_t xa = wa[tt >> 2] >> (8 * (tt & 3)), xb = wb[tt >> 2] >> (8 * (tt & 3));
-              const uint32_t va = pack_u16x2(lds16(rw + 2u * (xa & 15u)), lds16(rw + 2u * ((xa >> 4) & 15u)));
-              const uint32_t vb = pack_u16x2(lds16(rw + 2u * (xb & 15u)), lds16(rw + 2u * ((xb >> 4) & 15u)));
-              sts32((tl4 ^ (16u * (tt & 7))) + 256u * tt, va);
-              sts32((tl4 ^ (16u * ((tt & 7) ^ 4))) + 128u + 256u * tt, vb);
+          for (int u = 0; u < DS * NLV / 32; ++u) ws.vlut[lane + 32 * u] = lv[u];
+          __syncwarp();
+          vbase = smem_u32(ws.vlut);
+        }
+        vbase += 2u * NLV * (uint32_t)t;  // token t's table
+        vlow = ((2u * NLV * (uint32_t)t) & 0xFFu) * 0x01010101u;
+      }
+      {
+        const uint8_t* rowp = ws.raw[st] + DS * RBK + t * RBV + half * (RBV / 2);
+        if (BV == 4) {
+          const uint4 ca = *reinterpret_cast<const uint4*>(rowp + 16 * cx0);
+          const uint4 cb = *reinterpret_cast<const uint4*>(rowp + 16 * (cx0 ^ 1));
+          const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sts128(tw4 ^ (64u * j + 16u * i), lut8_nib<0>(wv[4 * j + i], vlow, vbase, 0u));
+        } else {
+          const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
+          const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
+          if (vshared) {  // one level-pair table for every token
+            const uint32_t pb = smem_u32(sm.vpair);
+#pragma unroll
+            for (int w4 = 0; w4 < 4; ++w4) {
+              uint4 o0, o1;
+              lut8_pair<0>(wv[w4], 0u, pb, 0u, o0, o1);
+              sts128(tw ^ (32u * w4), o0);
+              sts128(tw ^ (32u * w4 + 16u), o1);
             }
           } else {
-            const uint4 ca = *reinterpret_cast<const uint4*>(vc + 16 * lane);
-            const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
 #pragma unroll
-            for (int tt = 0; tt < DS; ++tt) {
-              const uint32_t rw = vrow + 8u * tt;
-              const uint32_t xa = wa[tt >> 2] >> (8 * (tt & 3));
-              const uint2 v = make_uint2(pack_u16x2(lds16(rw + 2u * (xa & 3u)), lds16(rw + 2u * ((xa >> 2) & 3u))),
-                                         pack_u16x2(lds16(rw + 2u * ((xa >> 4) & 3u)), lds16(rw + 2u * ((xa >> 6) & 3u))));
-              sts64((tl2 ^ (16u * (tt & 7))) + 256u * tt, v);
+            for (int w4 = 0; w4 < 4; ++w4) {
+              uint4 o0, o1;
+              lut16_crumb<0>(wv[w4], vlow, vbase, 0u, o0, o1);
+              sts128(tw ^ (32u * w4), o0);
+              sts128(tw ^ (32u * w4 + 16u), o1);
             }
           }
         }
@@ -942,10 +1002,6 @@ static int prepare_decode(DecodeParams& p, const hx_pool_layer* pool, const hx_l
   if (pool->head_size != DD || pool->block_size != DS || group > 8) return HX_ERR_UNSUPPORTED;
   if ((pool->bits_k != 2 && pool->bits_k != 4) || (pool->bits_v != 2 && pool->bits_v != 4)) return HX_ERR_ARG;
   if (!sc->k_poles || !sc->v_poles) return HX_ERR_ARG;
-  // the level tables of hx_scales_prepare, built for this pool's code widths
-  if (!sc->dec_tabs || sc->tab_bits != (pool->bits_k | (pool->bits_v << 8)) ||
-      (reinterpret_cast<uintptr_t>(sc->dec_tabs) & 15u))
-    return HX_ERR_ARG;
   if (sc->levels_k < 1 || sc->levels_v < 1 || sc->levels_k > (1 << pool->bits_k) ||
       sc->levels_v > (1 << pool->bits_v) || sc->t_cal < 1)
     return HX_ERR_ARG;

@@ -172,15 +172,14 @@ HX_DEVINL void atomic_max_f16(uint16_t* addr, uint16_t v, uint32_t* err) {
   set_err(err, HX_DEV_ERR_TIMEOUT);
 }
 
-// Write slot t's packed codes from the warp's staged byte codes into a
-// column-major block (byte j of slot t at j * S + t).
-HX_DEVINL void store_row(uint8_t* block, int t, int S, const uint8_t* codes, int D, int bits) {
+// Write one packed code row from the warp's staged byte codes.
+HX_DEVINL void store_row(uint8_t* dst, const uint8_t* codes, int D, int bits) {
   const int per = 8 / bits;
   const int nbytes = D / per;
   for (int b = lane_id(); b < nbytes; b += 32) {
     uint32_t v = 0;
     for (int j = 0; j < per; ++j) v |= (uint32_t)(codes[b * per + j] & ((1 << bits) - 1)) << (bits * j);
-    block[(int64_t)b * S + t] = (uint8_t)v;
+    dst[b] = (uint8_t)v;
   }
 }
 
@@ -324,7 +323,7 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
       m[k] = __ballot_sync(0xffffffffu, out);
     }
     __syncwarp();
-    store_row(seg, t, S, sc8, D, pool.bits_k);
+    store_row(seg + (int64_t)t * rbk, sc8, D, pool.bits_k);
     append_row<KD>(pool, LKs, m, xb, t, err);
     __syncwarp();
 
@@ -352,7 +351,7 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
       m[k] = __ballot_sync(0xffffffffu, out);
     }
     __syncwarp();
-    store_row(seg + (int64_t)S * rbk, t, S, sc8, D, pool.bits_v);
+    store_row(seg + (int64_t)S * rbk + (int64_t)t * rbv, sc8, D, pool.bits_v);
     append_row<KD>(pool, LVs, m, xb, t, err);
     __syncwarp();
   }
@@ -383,10 +382,9 @@ __global__ void __launch_bounds__(128) pack_append_kernel(hx_pool_layer pool, hx
 // ---------------------------------------------------------------------------
 // staging unpack: one block per (selected page, head)
 
-// Code of channel d, slot t in a column-major block of S slots.
-HX_DEVINL int code_at(const uint8_t* block, int S, int t, int d, int bits) {
+HX_DEVINL int code_at(const uint8_t* rowp, int d, int bits) {
   const int per = 8 / bits;
-  return (block[(d / per) * S + t] >> ((d % per) * bits)) & ((1 << bits) - 1);
+  return (rowp[d / per] >> ((d % per) * bits)) & ((1 << bits) - 1);
 }
 
 __global__ void __launch_bounds__(128) unpack_pages_kernel(hx_pool_layer pool, hx_layer_scales sc,
@@ -408,8 +406,8 @@ __global__ void __launch_bounds__(128) unpack_pages_kernel(hx_pool_layer pool, h
   uint16_t* tv = tile + S * D;
   for (int e = threadIdx.x; e < S * D; e += blockDim.x) {
     int t = e / D, d = e % D;
-    int ck = code_at(seg, S, t, d, pool.bits_k);
-    int cv = code_at(seg + S * rbk, S, t, d, pool.bits_v);
+    int ck = code_at(seg + t * rbk, d, pool.bits_k);
+    int cv = code_at(seg + S * rbk + t * rbv, d, pool.bits_v);
     // a code >= levels can only come from an unwritten slot; it reads level 0
     ck = ck < sc.levels_k ? ck : 0;
     cv = cv < sc.levels_v ? cv : 0;

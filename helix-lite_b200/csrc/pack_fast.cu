@@ -22,6 +22,8 @@
 // is not strictly increasing and finite gets X = -inf. An element with
 // !(x < X) (at or above the bound, +inf, NaN) takes the scan itself, in fp32
 // from the poles, so every code is the reference's.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace hx {
@@ -93,50 +95,6 @@ __global__ void scales_prepare_kernel(int mode, const uint16_t* poles, int64_t r
 #pragma unroll
     for (int l = 0; l < 16; ++l) out[r * 16 + l] = (uint32_t)t[l] * 0x00010001u;
   }
-}
-
-// Decode tables of one layer, per KV head 96 KB laid out exactly as the decode
-// kernel keeps them in shared memory (24576 words):
-//   words [0, 16384): K, 256 rows (code byte b) x 64 words. nuq4: word 64 b + P
-//     = levels of channels 2P, 2P+1 for the two nibbles of b (pair tables, one
-//     per channel pair in its own bank column); nuq2: words 64 b + 2Q, +1 =
-//     levels of channels 4Q .. 4Q+3 for the four crumbs of b (quad tables).
-//   words [16384, 24576): V beyond t_cal (row t_cal - 1 of every token), 256
-//     rows x 32 words, the byte's levels replicated: nuq4 32 copies of the
-//     pair entry, nuq2 16 copies of the 8-byte quad entry.
-// Codes at or above a table's level count read 0.
-constexpr int kDecTabWords = 24576, kDecKWords = 16384;
-
-HX_DEVINL uint16_t pole_or0(const uint16_t* row, int L, int c) { return c < L ? row[c] : (uint16_t)0; }
-
-__global__ void decode_tables_kernel(const hx_layer_scales sc, int H, int bits_k, int bits_v, uint32_t* tabs) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (int64_t)H * kDecTabWords) return;
-  const int h = (int)(idx / kDecTabWords), w = (int)(idx % kDecTabWords);
-  uint32_t v;
-  if (w < kDecKWords) {
-    const int b = w >> 6, col = w & 63;
-    const int Lk = sc.levels_k;
-    const uint16_t* kp = sc.k_poles + (int64_t)h * 128 * Lk;
-    if (bits_k == 4) {  // pair col: channels 2 col, 2 col + 1
-      v = pack_u16x2(pole_or0(kp + (2 * col) * Lk, Lk, b & 15), pole_or0(kp + (2 * col + 1) * Lk, Lk, b >> 4));
-    } else {            // quad col >> 1: channels 4q .. 4q+3, word half col & 1
-      const int q = col >> 1, e = col & 1;
-      v = pack_u16x2(pole_or0(kp + (4 * q + 2 * e) * Lk, Lk, (b >> (4 * e)) & 3),
-                     pole_or0(kp + (4 * q + 2 * e + 1) * Lk, Lk, (b >> (4 * e + 2)) & 3));
-    }
-  } else {
-    const int r = w - kDecKWords, b = r >> 5, col = r & 31;
-    const int Lv = sc.levels_v;
-    const uint16_t* vt = sc.v_poles + ((int64_t)h * sc.t_cal + (sc.t_cal - 1)) * Lv;
-    if (bits_v == 4) {
-      v = pack_u16x2(pole_or0(vt, Lv, b & 15), pole_or0(vt, Lv, b >> 4));
-    } else {
-      const int e = col & 1;
-      v = pack_u16x2(pole_or0(vt, Lv, (b >> (4 * e)) & 3), pole_or0(vt, Lv, (b >> (4 * e + 2)) & 3));
-    }
-  }
-  tabs[idx] = v;
 }
 
 // ---- fp16-pair helpers ---------------------------------------------------------
@@ -359,34 +317,41 @@ __device__ __noinline__ ScanFix scan_fix(const uint16_t* pbase, int pstride, int
 // counts the runs each (head, page) receives. One warp per (window of 16
 // input tokens, head). A run is a maximal stretch of input tokens filling
 // consecutive slots of one page; each run starting in the window is processed
-// whole (it may reach past the window's end). Lane l owns channels 4l .. 4l+3
-// of every token of the run: one 8-byte load per token row, codes by
-// bisection (K: the thresholds of the lane's channel pairs in registers; V:
-// each token's row of thresholds from shared memory), and the lane's byte
-// column(s) of the page's column-major code block (nuq4: pairs 2l and 2l+1,
-// nuq2: quad l) written as one 16-byte store per column for a whole page.
+// whole (it may reach past the window's end). One load of the window's slots
+// (and positions) gives every run's leader, length and V rows. Per run, one
+// round of asynchronous copies brings the run's rows (lane l: channels
+// 4l .. 4l+3 of each token), V's threshold rows and, for a page with one run,
+// its record and stats into shared memory; then the codes come by bisection
+// (K: the thresholds of the lane's channel pairs in registers; V: each token's
+// row from shared memory) and each token's packed row is stored (nuq4: two
+// bytes per lane, nuq2: one).
 //
 // Each directory record's last word is rows (bits 0-7, slots written) |
 // runs (bits 8-30, this launch's run count from the pre-pass) | lock (bit
-// 31). A page with one run belongs to its warp: record and stats are read
-// beside the data loads and written back plainly. A page with several runs
-// (tokens of the page not contiguous in the input) is updated one run at a
-// time under the record's lock, so no list entry or stat is lost.
+// 31). A page with one run belongs to its warp and is written back plainly.
+// A page with several runs (tokens of the page not contiguous in the input)
+// is updated one run at a time under the record's lock, so no list entry or
+// stat is lost.
 constexpr int PF_D = 128, PF_S = 16;
 constexpr int PF_STAGE = PF_S * PF_D;  // one run's outlier entries, staged (every element at worst)
 constexpr uint32_t kRunsOne = 1u << 8, kRunsMask = 0x7FFFFF00u, kRowsMask = 0xFFu;
 
+struct __align__(16) PackWarpSmem {
+  uint32_t rows[PF_S][PF_D / 2];  // the run's rows of this head (fp16 pairs), lane l at words 2l, 2l+1
+  uint32_t vt[PF_S][20];          // V: per slot 16 thresholds + band (80-byte rows)
+  uint32_t rec[4];                // an exclusive page's record
+  uint32_t st[32][4];             // and its stats: lane l's min (2 words) then max (2 words)
+  uint32_t ent[PF_STAGE];         // the run's outlier entries
+};
+
 template <int BITS, bool IS_V>
-__global__ void __launch_bounds__(128, IS_V ? 5 : 4)
+__global__ void __launch_bounds__(128, 4)
     pack_list_kernel(const hx_pool_layer pool, const hx_layer_scales sc, const uint16_t* __restrict__ x,
                      const int64_t* __restrict__ slots, const int64_t* __restrict__ abspos, int T, uint32_t* err) {
-  // tokens per batch: K's nuq4 thresholds take 32 registers, so fewer tokens in flight
-  constexpr int BT = (!IS_V && BITS == 4) ? 4 : 8;
-  __shared__ uint32_t s_ent[4][PF_STAGE];                  // a run's outlier entries
-  __shared__ __align__(16) uint32_t s_pre[4][4 + 4 * 32];  // an exclusive page's record and stats
-  __shared__ __align__(16) uint32_t s_vt[IS_V ? 4 : 1][IS_V ? 16 * 20 : 1];  // V: per slot 16 thresholds + band (80-byte rows)
+  constexpr int RB = PF_D * BITS / 8;  // code bytes per slot
+  extern __shared__ __align__(16) uint8_t pf_smem[];  // 4 warps' PackWarpSmem
   const int lane = lane_id(), warp = threadIdx.x >> 5;
-  uint32_t* sent = s_ent[warp];
+  PackWarpSmem& ws = reinterpret_cast<PackWarpSmem*>(pf_smem)[warp];
   const int H = pool.num_kv_heads, NB = pool.num_blocks, Tc = sc.t_cal;
   const int64_t seg_bytes = (int64_t)PF_S * PF_D * (pool.bits_k + pool.bits_v) / 8;
   const int64_t blk_off = IS_V ? (int64_t)PF_S * PF_D * pool.bits_k / 8 : 0;
@@ -396,19 +361,21 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
   const int win = (int)(wg / H), h = (int)(wg % H);
   const int i0 = win * 16;
 
-  // run leaders of the window
-  bool lead = false;
-  if (lane < 16 && i0 + lane < T) {
-    const int64_t s = slots[i0 + lane];
-    if (s >= 0) {
-      lead = true;
-      if (i0 + lane > 0) {
-        const int64_t sp = slots[i0 + lane - 1];
-        if (sp >= 0 && sp + 1 == s && (s % PF_S) != 0) lead = false;
-      }
+  // slots (and V positions) of tokens i0 - 1 .. i0 + 30: lane j holds token i0 - 1 + j
+  const int tj = i0 - 1 + lane;
+  const int64_t sj = (tj >= 0 && tj < T) ? slots[tj] : -1;
+  int64_t pj = 0;
+  if (IS_V && tj >= 0 && tj < T) {
+    pj = abspos[tj];
+    if (pj < 0 && sj >= 0) {
+      set_err(err, HX_DEV_ERR_BOUNDS);
+      pj = 0;
     }
   }
-  uint32_t leaders = __ballot_sync(0xffffffffu, lead);
+  const int64_t sprev = __shfl_up_sync(0xffffffffu, sj, 1);
+  const bool lead = lane >= 1 && lane <= 16 && sj >= 0 &&
+                    !(sprev >= 0 && sprev + 1 == sj && (sj % PF_S) != 0);
+  uint32_t leaders = __ballot_sync(0xffffffffu, lead) >> 1;  // bit r: token i0 + r leads a run
   if (!leaders) return;
   const int L = IS_V ? sc.levels_v : sc.levels_k;
 
@@ -432,7 +399,7 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
     const int r = __ffs(leaders) - 1;
     leaders &= leaders - 1;
     const int i = i0 + r;
-    const int64_t s0 = slots[i];
+    const int64_t s0 = __shfl_sync(0xffffffffu, sj, r + 1);
     const int64_t pg64 = s0 / PF_S;
     if (pg64 >= NB) {
       if (lane == 0) set_err(err, HX_DEV_ERR_BOUNDS);
@@ -440,50 +407,49 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
     }
     const int pg = (int)pg64, t0 = (int)(s0 % PF_S);
     int n;
-    {
-      bool ok = false;
-      if (lane >= 1 && lane < PF_S - t0 && i + lane < T) ok = slots[i + lane] == s0 + lane;
-      const uint32_t m = __ballot_sync(0xffffffffu, ok) | 1u;
+    {  // lanes r + 1 + k, k >= 1, continue the run while their slots follow s0
+      const int k = lane - (r + 1);
+      const bool ok = k >= 1 && t0 + k < PF_S && sj == s0 + k;
+      const uint32_t m = (__ballot_sync(0xffffffffu, ok) >> (r + 1)) | 1u;
       n = __ffs(~m) - 1;
+      if (r + 1 + n > 31) n = 31 - r;  // tokens past the loaded ones: the next window's leaders are not affected
     }
     uint8_t* blk = pool.codes + ((int64_t)h * NB + pg) * seg_bytes + blk_off;
     uint32_t* rec = pool.dir + (((int64_t)h * NB + pg) * 2 + (IS_V ? 1 : 0)) * 4;
     uint16_t* st = pool.stats + ((int64_t)h * NB + pg) * 2 * PF_D + 4 * lane;
     const bool excl = (__ldcg(rec + 3) & kRunsMask) == kRunsOne;
-    // an exclusive page's record and stats are fetched now, into shared
-    // memory (no registers held across the compute)
-    uint32_t* s_rec = s_pre[warp];  // [0..3] record, [4 + 4 lane ..] stats min / max of the lane's channels
-    if (excl) {
-      if (lane == 0) cp_async_16(s_rec, rec);
-      if (!IS_V) {
-        cp_async_8(s_rec + 4 + 4 * lane, st);
-        cp_async_8(s_rec + 6 + 4 * lane, st + PF_D);
-      }
-      cp_async_commit();
-    }
+
+    // ---- one round of asynchronous copies: rows, V threshold rows, record, stats
+    __syncwarp();  // the previous run's readers of the buffers are done
+#pragma unroll
+    for (int j = 0; j < PF_S; ++j)
+      if (j < n) cp_async_8(&ws.rows[j][2 * lane], x + ((int64_t)(i + j) * H + h) * PF_D + 4 * lane);
+    uint32_t vband = 0;  // V: lane j's slot band, staged after the copies are issued
     if (IS_V) {
-      // thresholds and band of the run's V rows: lane 2j + e stages half of slot j's
-      __syncwarp();
       const int j = lane >> 1, e = lane & 1;
+      const int64_t pos = __shfl_sync(0xffffffffu, pj, (r + 1 + j) & 31);
       if (j < n) {
-        int64_t p = abspos[i + j];
-        if (p < 0) {
-          set_err(err, HX_DEV_ERR_BOUNDS);
-          p = 0;
-        }
-        const int64_t rr = (int64_t)h * Tc + (p < Tc ? p : Tc - 1);
+        const int64_t rr = (int64_t)h * Tc + (pos < Tc ? pos : Tc - 1);
         const uint4* tr = reinterpret_cast<const uint4*>(sc.v_thresh) + rr * 4 + 2 * e;
-        uint32_t* dstv = s_vt[warp] + j * 20;
-        const uint4 a = __ldg(tr), b = __ldg(tr + 1);
-        reinterpret_cast<uint4*>(dstv)[2 * e] = a;
-        reinterpret_cast<uint4*>(dstv)[2 * e + 1] = b;
-        if (e == 0) {
-          dstv[16] = (uint32_t)sc.v_upper[rr] * 0x00010001u;
-          dstv[17] = (uint32_t)sc.v_lower[rr] * 0x00010001u;
-        }
+        cp_async_16(&ws.vt[j][8 * e], tr);
+        cp_async_16(&ws.vt[j][8 * e + 4], tr + 1);
+        vband = e == 0 ? (uint32_t)sc.v_upper[rr] : (uint32_t)sc.v_lower[rr];
       }
-      __syncwarp();
     }
+    if (excl) {
+      if (lane == 0) cp_async_16(ws.rec, rec);
+      if (!IS_V) {
+        cp_async_8(&ws.st[lane][0], st);
+        cp_async_8(&ws.st[lane][2], st + PF_D);
+      }
+    }
+    cp_async_commit();
+    if (IS_V) {
+      const int j = lane >> 1, e = lane & 1;
+      if (j < n) ws.vt[j][16 + e] = vband * 0x00010001u;
+    }
+    cp_async_wait_all();
+    __syncwarp();
 
     uint32_t cmina = 0x001F001Fu, cminb = 0x001F001Fu, cmaxa = 0u, cmaxb = 0u;  // K code range (+1 for max)
     float emin[4], emax[4];  // K outliers and scanned elements, exact values
@@ -492,30 +458,21 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
       emin[k] = __int_as_float(0x7f800000);
       emax[k] = __int_as_float(0xff800000);
     }
-    uint32_t colA[4] = {0u, 0u, 0u, 0u}, colB[4] = {0u, 0u, 0u, 0u};  // byte j = run token j
-    // batches of BT tokens; a batch's outlier entries are staged (lane-major)
-    // after the previous batches' while its values are in registers
-    int tot = 0;
+    int tot = 0;  // outlier entries staged so far (lane-major within each 8-token batch)
 #pragma unroll 1
-    for (int hb = 0; hb < PF_S / BT; ++hb) {
-      const int j0 = BT * hb;
+    for (int hb = 0; hb < 2; ++hb) {
+      const int j0 = 8 * hb;
       if (j0 >= n) break;
-      uint2 xs[BT];
-#pragma unroll
-      for (int jj = 0; jj < BT; ++jj)
-        xs[jj] = j0 + jj < n ? *reinterpret_cast<const uint2*>(x + ((int64_t)(i + j0 + jj) * H + h) * PF_D + 4 * lane)
-                             : make_uint2(0u, 0u);
       uint32_t outm = 0;
-      uint32_t wA[BT / 4], wB[BT / 4];  // the batch's column bytes (byte jj at word jj / 4)
 #pragma unroll
-      for (int u = 0; u < BT / 4; ++u) wA[u] = wB[u] = 0u;
-#pragma unroll
-      for (int jj = 0; jj < BT; ++jj) {
-        if (j0 + jj < n) {
-          const uint32_t xa = xs[jj].x, xb = xs[jj].y;
+      for (int jj = 0; jj < 8; ++jj) {
+        const int j = j0 + jj;
+        if (j < n) {
+          const uint2 xr = *reinterpret_cast<const uint2*>(&ws.rows[j][2 * lane]);
+          const uint32_t xa = xr.x, xb = xr.y;
           uint32_t ca, cb, oa, ob, sa, sb;
           if (IS_V) {
-            const uint32_t* vr = s_vt[warp] + (j0 + jj) * 20;
+            const uint32_t* vr = ws.vt[j];
             uint32_t tv[16];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -541,9 +498,9 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
           if (__any_sync(0xffffffffu, (sa | sb) != 0u)) {
             const uint16_t* pb;
             if (IS_V) {
-              int64_t p = abspos[i + j0 + jj];
-              p = p < 0 ? 0 : p;
-              pb = sc.v_poles + ((int64_t)h * Tc + (p < Tc ? p : Tc - 1)) * L;
+              int64_t pos = abspos[i + j];
+              pos = pos < 0 ? 0 : pos;
+              pb = sc.v_poles + ((int64_t)h * Tc + (pos < Tc ? pos : Tc - 1)) * L;
             } else {
               pb = sc.k_poles + ((int64_t)h * PF_D + 4 * lane) * L;
             }
@@ -565,27 +522,18 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
             cmaxb = umax2(cmaxb, (cb + 0x00010001u) & ~exb);
           }
           outm |= ((oa & 1u) | ((oa >> 15) & 2u) | ((ob & 1u) << 2) | ((ob >> 13) & 8u)) << (4 * jj);
-          const int sh = 8 * (jj & 3);
+          // the token's packed row: nuq4 bytes 2l, 2l+1; nuq2 byte l
+          uint8_t* row = blk + (t0 + j) * RB;
           if (BITS == 4) {
-            wA[jj >> 2] |= ((ca & 0xFu) | ((ca >> 12) & 0xF0u)) << sh;
-            wB[jj >> 2] |= ((cb & 0xFu) | ((cb >> 12) & 0xF0u)) << sh;
+            const uint32_t w = (ca & 0xFu) | ((ca >> 12) & 0xF0u) | ((cb & 0xFu) << 8) | ((cb >> 4) & 0xF000u);
+            *reinterpret_cast<uint16_t*>(row + 2 * lane) = (uint16_t)w;
           } else {
-            wA[jj >> 2] |= ((ca & 3u) | ((ca >> 14) & 0xCu) | ((cb & 3u) << 4) | ((cb >> 10) & 0xC0u)) << sh;
+            row[lane] = (uint8_t)((ca & 3u) | ((ca >> 14) & 0xCu) | ((cb & 3u) << 4) | ((cb >> 10) & 0xC0u));
           }
         }
       }
-      // the batch's words into the run's columns (static indices: predicated moves)
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-#pragma unroll
-        for (int u = 0; u < BT / 4; ++u)
-          if (q == j0 / 4 + u) {
-            colA[q] = wA[u];
-            colB[q] = wB[u];
-          }
       // the batch's entries (lane-major: channel group, then token, then
-      // channel) staged while the values are in registers; K's also enter
-      // the page stats
+      // channel) staged; K's also enter the page stats
       int tb;
       const int base = tot + warp_excl_scan(__popc(outm), tb);
       {
@@ -594,11 +542,11 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
         while (m) {
           const int b = __ffs(m) - 1;
           m &= m - 1;
-          const int jj = b >> 2, k = b & 3;
-          const uint16_t xb = kval_batch<BT>(xs, jj, k);
-          sent[q++] = (uint32_t)xb | ((uint32_t)(4 * lane + k) << 16) | ((uint32_t)(t0 + j0 + jj) << 24);
+          const int j = j0 + (b >> 2), k = b & 3;
+          const uint16_t xv = reinterpret_cast<const uint16_t*>(&ws.rows[j][2 * lane])[k];
+          ws.ent[q++] = (uint32_t)xv | ((uint32_t)(4 * lane + k) << 16) | ((uint32_t)(t0 + j) << 24);
           if (!IS_V) {
-            const float xf = h2f(xb);
+            const float xf = h2f(xv);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               if (kk == k) {
@@ -611,32 +559,14 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
       tot += tb;
     }
 
-    // ---- the lane's byte columns of the code block
-    {
-      const int c0 = BITS == 4 ? 2 * lane : lane;
-      if (t0 == 0 && n == PF_S) {
-        reinterpret_cast<uint4*>(blk + c0 * PF_S)[0] = make_uint4(colA[0], colA[1], colA[2], colA[3]);
-        if (BITS == 4) reinterpret_cast<uint4*>(blk + (c0 + 1) * PF_S)[0] = make_uint4(colB[0], colB[1], colB[2], colB[3]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < PF_S; ++j)
-          if (j < n) {
-            blk[c0 * PF_S + t0 + j] = (uint8_t)(colA[j >> 2] >> (8 * (j & 3)));
-            if (BITS == 4) blk[(c0 + 1) * PF_S + t0 + j] = (uint8_t)(colB[j >> 2] >> (8 * (j & 3)));
-          }
-      }
-    }
-
     // ---- the page's list (and K stats)
     uint4 rc;
     uint2 smin = make_uint2(0u, 0u), smax = smin;
     if (excl) {
-      cp_async_wait_all();
-      __syncwarp();
-      rc = *reinterpret_cast<const uint4*>(s_rec);
+      rc = *reinterpret_cast<const uint4*>(ws.rec);
       if (!IS_V) {
-        smin = *reinterpret_cast<const uint2*>(s_rec + 4 + 4 * lane);
-        smax = *reinterpret_cast<const uint2*>(s_rec + 6 + 4 * lane);
+        smin = make_uint2(ws.st[lane][0], ws.st[lane][1]);
+        smax = make_uint2(ws.st[lane][2], ws.st[lane][3]);
       }
     } else {
       if (!page_lock(rec + 3, err)) continue;
@@ -657,7 +587,7 @@ __global__ void __launch_bounds__(128, IS_V ? 5 : 4)
     __syncwarp();
     if (ok) {
       uint32_t* de = pool.arena + LR.off + LR.cnt;
-      for (int q = lane; q < tot; q += 32) de[q] = sent[q];
+      for (int q = lane; q < tot; q += 32) de[q] = ws.ent[q];
       LR.cnt += tot;
     }
     if (!IS_V) {  // K page stats: the run's reconstructed min / max folded into the page's
@@ -746,35 +676,42 @@ int hx_pack_fast_launch(cudaStream_t s, const hx_pool_layer* pool, const hx_laye
   const int64_t blocks = (warps + 3) / 4;
   const int64_t cthreads = (int64_t)T * pool->num_kv_heads;
   if (blocks > 0x7fffffff || (cthreads + 255) / 256 > 0x7fffffff) return HX_ERR_ARG;
+  const size_t smem = 4 * sizeof(PackWarpSmem);
+  {
+    // once per device: the kernels' dynamic shared memory above the default 48 KB
+    static std::atomic<bool> attr_set[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_ERR_LAUNCH;
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
+      if (cudaFuncSetAttribute(pack_list_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ||
+          cudaFuncSetAttribute(pack_list_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ||
+          cudaFuncSetAttribute(pack_list_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ||
+          cudaFuncSetAttribute(pack_list_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem))
+        return HX_ERR_LAUNCH;
+      attr_set[dev].store(true, std::memory_order_release);
+    }
+  }
   pack_count_runs_kernel<<<(unsigned)((cthreads + 255) / 256), 256, 0, s>>>(*pool, slots, T);
   const dim3 grid((unsigned)blocks), block(128);
-  if (pool->bits_k == 4) pack_list_kernel<4, false><<<grid, block, 0, s>>>(*pool, *sc, key, slots, abspos, T, dev_err);
-  else pack_list_kernel<2, false><<<grid, block, 0, s>>>(*pool, *sc, key, slots, abspos, T, dev_err);
-  if (pool->bits_v == 4) pack_list_kernel<4, true><<<grid, block, 0, s>>>(*pool, *sc, value, slots, abspos, T, dev_err);
-  else pack_list_kernel<2, true><<<grid, block, 0, s>>>(*pool, *sc, value, slots, abspos, T, dev_err);
+  if (pool->bits_k == 4) pack_list_kernel<4, false><<<grid, block, smem, s>>>(*pool, *sc, key, slots, abspos, T, dev_err);
+  else pack_list_kernel<2, false><<<grid, block, smem, s>>>(*pool, *sc, key, slots, abspos, T, dev_err);
+  if (pool->bits_v == 4) pack_list_kernel<4, true><<<grid, block, smem, s>>>(*pool, *sc, value, slots, abspos, T, dev_err);
+  else pack_list_kernel<2, true><<<grid, block, smem, s>>>(*pool, *sc, value, slots, abspos, T, dev_err);
   HX_LAUNCH_CHECK();
   return HX_OK;
 }
 
 extern "C" {
 
-HX_API int hx_scales_prepare(void* stream, const hx_layer_scales* sc, int32_t H, int32_t D, int32_t bits_k,
-                             int32_t bits_v, uint32_t* k_thresh, uint32_t* v_thresh, uint32_t* dec_tabs) {
+HX_API int hx_scales_prepare(void* stream, const hx_layer_scales* sc, int32_t H, int32_t D, uint32_t* k_thresh,
+                             uint32_t* v_thresh) {
   if (!sc || !sc->k_poles || !sc->v_poles || H <= 0 || D <= 0 || (D & 1) || !k_thresh || !v_thresh) return HX_ERR_ARG;
   if (sc->levels_k < 1 || sc->levels_k > 16 || sc->levels_v < 1 || sc->levels_v > 16 || sc->t_cal < 1)
-    return HX_ERR_ARG;
-  if ((bits_k != 2 && bits_k != 4) || (bits_v != 2 && bits_v != 4) || sc->levels_k > (1 << bits_k) ||
-      sc->levels_v > (1 << bits_v))
     return HX_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int64_t rk = (int64_t)H * D, rv = (int64_t)H * sc->t_cal;
   scales_prepare_kernel<<<(unsigned)((rk + 127) / 128), 128, 0, s>>>(0, sc->k_poles, rk, sc->levels_k, k_thresh);
   scales_prepare_kernel<<<(unsigned)((rv + 127) / 128), 128, 0, s>>>(1, sc->v_poles, rv, sc->levels_v, v_thresh);
-  if (dec_tabs) {
-    if (D != 128) return HX_ERR_UNSUPPORTED;
-    const int64_t nw = (int64_t)H * kDecTabWords;
-    decode_tables_kernel<<<(unsigned)((nw + 255) / 256), 256, 0, s>>>(*sc, H, bits_k, bits_v, dec_tabs);
-  }
   HX_LAUNCH_CHECK();
   return HX_OK;
 }

@@ -29,8 +29,8 @@ c_vp, c_i32, c_i64, c_f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, cty
 class LayerScales(ctypes.Structure):
     _fields_ = [("k_poles", c_vp), ("k_upper", c_vp), ("k_lower", c_vp),
                 ("v_poles", c_vp), ("v_upper", c_vp), ("v_lower", c_vp),
-                ("levels_k", c_i32), ("levels_v", c_i32), ("t_cal", c_i32), ("tab_bits", c_i32),
-                ("k_thresh", c_vp), ("v_thresh", c_vp), ("dec_tabs", c_vp)]
+                ("levels_k", c_i32), ("levels_v", c_i32), ("t_cal", c_i32), ("reserved", c_i32),
+                ("k_thresh", c_vp), ("v_thresh", c_vp)]
 
 
 class PoolLayer(ctypes.Structure):
@@ -45,7 +45,7 @@ _SIGS = {
     "hx_pool_init": (c_i32, [c_vp, _P(PoolLayer)]),
     "hx_pool_reset_pages": (c_i32, [c_vp, _P(PoolLayer), c_vp, c_i32, c_vp]),
     "hx_pack_append": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_vp, c_vp, c_vp, c_i32, c_vp]),
-    "hx_scales_prepare": (c_i32, [c_vp, _P(LayerScales), c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "hx_scales_prepare": (c_i32, [c_vp, _P(LayerScales), c_i32, c_i32, c_vp, c_vp]),
     "hx_unpack_pages": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_vp, c_i32, c_vp, c_vp, c_vp]),
     "hx_nuq_pack_dense": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                                   c_vp, c_vp, c_vp]),
@@ -106,7 +106,7 @@ def lib():
 
 
 # kernel launches each entry point makes (bench.py counts launches with this)
-LAUNCHES = {"hx_scales_prepare": 3, "hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 1, "hx_unpack_pages": 1,
+LAUNCHES = {"hx_scales_prepare": 2, "hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 1, "hx_unpack_pages": 1,
             "hx_nuq_pack_dense": 1, "hx_nuq_unpack_dense": 1, "hx_nuq_quantize_flat": 2,
             "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": 1, "hx_quest_threshold_slices": 1,
             "hx_quest_compact": 1, "hx_quest_lists": 2, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_merge_partials": 1, "hx_merge_gathered": 1,

@@ -5,10 +5,8 @@ signatures. Storage is the packed format of include/helix_kv.h rather than
 one byte per code plus dense fp16 outliers (compact_pool.py:426-441):
 
   codes   (H, NB, seg) uint8 per layer; a (head, page) segment is the page's
-          K codes then its V codes, 4 bits per code for up to 16 levels, 2
-          bits for up to 4; each block stores its slots' packed rows
-          column-major (byte j of slot t at j * S + t), so a byte column is
-          one channel pair (nuq4) or quad (nuq2) over the page
+          K code rows then its V code rows, 4 bits per code for up to 16
+          levels, 2 bits for up to 4
   stats   (H, NB, 2, D) fp16: running min / max of reconstructed K per page
           (exact in fp16; the reference keeps fp32 only for sm_86 atomics)
   dir     (H, NB, 2, 4) int32: {offset, capacity, count, rows} of the page's
@@ -143,7 +141,7 @@ class CompactKVPool:
             rb_k = D * lay.bits_k // 8
             rb = D * bits // 8
             base = 0 if kv == 0 else S * rb_k
-            rows = lay.codes[:, :, base:base + S * rb].reshape(H, self.num_blocks, rb, S).transpose(-1, -2)
+            rows = lay.codes[:, :, base:base + S * rb].reshape(H, self.num_blocks, S, rb)
             per = 8 // bits
             shifts = torch.arange(per, device=self.device, dtype=torch.uint8) * bits
             c = (rows.unsqueeze(-1) >> shifts) & ((1 << bits) - 1)

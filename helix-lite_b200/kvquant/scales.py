@@ -113,20 +113,15 @@ class KVScales:
               f16(vs.poles), f16(vs.upper_threshold), f16(vs.lower_threshold)]
         H, D, levels_k = (int(x) for x in ks.poles.shape)
         t_cal, levels_v = int(vs.poles.shape[1]), int(vs.poles.shape[-1])
-        st = LayerScales(*(t.data_ptr() for t in ts), levels_k, levels_v, t_cal, 0, None, None, None)
+        st = LayerScales(*(t.data_ptr() for t in ts), levels_k, levels_v, t_cal, 0, None, None)
         if D % 2 == 0 and levels_k <= 16 and levels_v <= 16:
             from hxlib import call, ptr, stream
-            bk, bv = (2 if levels_k <= 4 else 4), (2 if levels_v <= 4 else 4)   # the pool's code widths
             kt = torch.empty((H, D // 2, 16), dtype=torch.int32, device=dev)
             vt = torch.empty((H, t_cal, 16), dtype=torch.int32, device=dev)
-            tabs = torch.empty((H, 24576), dtype=torch.int32, device=dev) if D == 128 else None
             with torch.cuda.device(dev):
-                call("hx_scales_prepare", stream(dev), ctypes.byref(st), H, D, bk, bv, ptr(kt), ptr(vt), ptr(tabs))
+                call("hx_scales_prepare", stream(dev), ctypes.byref(st), H, D, ptr(kt), ptr(vt))
             st.k_thresh, st.v_thresh = kt.data_ptr(), vt.data_ptr()
             ts += [kt, vt]
-            if tabs is not None:
-                st.dec_tabs, st.tab_bits = tabs.data_ptr(), bk | (bv << 8)
-                ts.append(tabs)
         hit = (st, ts)
         self._dev_cache[key] = hit
         return hit

@@ -61,13 +61,11 @@ typedef struct hx_layer_scales {
   int32_t levels_k;          /* 2..16 */
   int32_t levels_v;          /* 2..16 */
   int32_t t_cal;             /* V positions >= t_cal use row t_cal - 1     */
-  int32_t tab_bits;          /* bits_k | bits_v << 8 of dec_tabs, 0 if none */
-  /* Written by hx_scales_prepare (device, 16-byte aligned), or NULL:
-   * hx_pack_append then takes its level-scan kernel.                     */
+  int32_t reserved;
+  /* Code thresholds written by hx_scales_prepare (device, 16-byte aligned),
+   * or NULL: hx_pack_append then takes its level-scan kernel.            */
   const uint32_t* k_thresh;  /* (H, D/2, 16) fp16 pairs                   */
   const uint32_t* v_thresh;  /* (H, t_cal, 16) fp16 duplicated in both halves */
-  /* Decode tables, (H, 24576) u32 per head; required by hx_decode_attn.  */
-  const uint32_t* dec_tabs;
 } hx_layer_scales;
 
 /*
@@ -136,17 +134,10 @@ HX_API int hx_pack_append(void* stream, const hx_pool_layer* pool, const hx_laye
  * Rows whose poles are not finite and strictly increasing get X = -inf; the
  * pack kernel runs the scan itself for every element with !(x < X). Layout:
  * k_thresh (H, D/2, 16) u32, half e of entry l of pair P from channel 2P+e;
- * v_thresh (H, t_cal, 16) u32, each entry's fp16 in both halves.
- * dec_tabs (optional, head_size 128): the decode's level tables for codes of
- * bits_k / bits_v bits, per head 96 KB: K pair (nuq4) or quad (nuq2) tables,
- * 256 rows by code byte x 64 words, word 64 b + P the levels of channel pair
- * P (nuq4; words 64 b + 2Q, +1 for quad Q, nuq2); then V beyond t_cal, 256
- * rows x 32 words of the byte's levels replicated (32 copies of the pair
- * entry, nuq4; 16 of the 8-byte quad entry, nuq2); set tab_bits = bits_k |
- * bits_v << 8. Computed once per scales (no reference counterpart: the
- * reference scans every level). */
-HX_API int hx_scales_prepare(void* stream, const hx_layer_scales* sc, int32_t H, int32_t D, int32_t bits_k,
-                             int32_t bits_v, uint32_t* k_thresh, uint32_t* v_thresh, uint32_t* dec_tabs);
+ * v_thresh (H, t_cal, 16) u32, each entry's fp16 in both halves. Computed once
+ * per scales (no reference counterpart: the reference scans every level). */
+HX_API int hx_scales_prepare(void* stream, const hx_layer_scales* sc, int32_t H, int32_t D,
+                             uint32_t* k_thresh, uint32_t* v_thresh);
 
 /* Dequantise whole pages to fp16 staging (NK, S, H, D) for K and V.
  * Replaces CompactKVPool.unpack_to_staging (compact_pool.py:492-537). */

@@ -8,11 +8,6 @@ bytes for nuq4, ``//4`` for nuq2). The build pins the order:
   * nuq2: byte i = code[4i] | code[4i+1] << 2 | code[4i+2] << 4 | code[4i+3] << 6
 
 applied along the last axis (head_dim) of a code array.
-
-In the pool a page segment holds these bytes column-major: byte j of the
-packed row of slot t sits at offset j * S + t of its K (or V) block, so one
-byte column holds a channel pair (nuq4) or quad (nuq2) for all S slots
-(``segment_from_rows`` / ``rows_from_segment``).
 """
 from __future__ import annotations
 
@@ -37,16 +32,3 @@ def unpack_codes(packed: np.ndarray, bits: int) -> np.ndarray:
     for j in range(per):
         out[..., j] = (p >> (bits * j)) & ((1 << bits) - 1)
     return out.reshape(p.shape[:-1] + (p.shape[-1] * per,))
-
-
-def segment_from_rows(rows: np.ndarray) -> np.ndarray:
-    """(..., S, RB) packed rows -> (..., RB * S) column-major block bytes."""
-    r = np.asarray(rows, dtype=np.uint8)
-    return np.ascontiguousarray(np.swapaxes(r, -1, -2)).reshape(r.shape[:-2] + (r.shape[-1] * r.shape[-2],))
-
-
-def rows_from_segment(block: np.ndarray, S: int) -> np.ndarray:
-    """(..., RB * S) column-major block bytes -> (..., S, RB) packed rows."""
-    b = np.asarray(block, dtype=np.uint8)
-    rb = b.shape[-1] // S
-    return np.ascontiguousarray(np.swapaxes(b.reshape(b.shape[:-1] + (rb, S)), -1, -2))

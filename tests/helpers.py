@@ -37,9 +37,9 @@ def gpu_codes(gpu, layer):
     lay = gpu.layers[layer]
     S, D = gpu.block_size, gpu.head_size
     rbk, rbv = D * lay.bits_k // 8, D * lay.bits_v // 8
-    from oracle.packing import rows_from_segment
     c = np16(lay.codes)
-    return rows_from_segment(c[:, :, :S * rbk], S), rows_from_segment(c[:, :, S * rbk:], S)
+    H, NB, _ = c.shape
+    return c[:, :, :S * rbk].reshape(H, NB, S, rbk), c[:, :, S * rbk:].reshape(H, NB, S, rbv)
 
 
 def gpu_outlier_array(gpu, layer):
