@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1-4 measurements")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="split-KV exchange: peer-memory merge kernel, or NCCL all-gather + merge")
     ap.add_argument("--profile", action="store_true", help="setup + warmup + steps only (for ncu)")
     return ap.parse_args()
 
@@ -293,7 +295,8 @@ def make_step(W, world, group, timing=None):
     o_loc = torch.empty((L, 1, H * G, D), dtype=torch.float32, device=dev)
     lse_loc = torch.empty((L, 1, H * G), dtype=torch.float32, device=dev)
     o_out = torch.empty((L, H * G, D), dtype=torch.float32, device=dev)
-    ex = Exchange(H * G, D, world, dev, group) if world > 1 else None
+    pex = W.get("pex")
+    ex = Exchange(H * G, D, world, dev, group) if world > 1 and pex is None else None
 
     def step(q_in=None):
         q_all = qs if q_in is None else q_in
@@ -304,13 +307,23 @@ def make_step(W, world, group, timing=None):
                                      scores=scores[li], thresh=thresh[li], slice_out=slices[li])
             if timing is not None:
                 timing["ev"][li][1].record()
-            # one GPU: the decode writes the layer's output in place
+            # one GPU: the decode writes the layer's output in place; several:
+            # its partials, into the exchange's row for the layer
+            if world == 1:
+                o_dst, lse_dst = o_out[li].view(1, H * G, D), lse_loc[li]
+            elif pex is not None:
+                o_dst, lse_dst = pex.o_view(li).view(1, H * G, D), pex.lse_view(li).view(1, H * G)
+            else:
+                o_dst, lse_dst = o_loc[li], lse_loc[li]
             fused.decode(pool, li, q_all[li], bt, sl, sel, page_begin=shard.page_begin, n_splits=W["ns"],
-                         o=o_loc[li] if world > 1 else o_out[li].view(1, H * G, D), lse=lse_loc[li])
+                         o=o_dst, lse=lse_dst)
             if timing is not None:
                 timing["ev"][li][2].record()
             if world > 1:
-                ex.merge(o_loc[li].view(H * G, D), lse_loc[li].view(H * G), o_out[li])
+                if pex is not None:
+                    pex.merge(li, o_out[li])
+                else:
+                    ex.merge(o_loc[li].view(H * G, D), lse_loc[li].view(H * G), o_out[li])
         return o_out
 
     return step
@@ -803,6 +816,26 @@ def run_ours(args):
 
     W = build_world(args, rank, world, device)
     L = args.layers
+    exchange = "none"
+    if world > 1:
+        # the layer exchange over peer memory (symmetric buffers, one merge
+        # kernel per layer); every rank takes it or none does
+        pex, err = None, ""
+        if args.exchange == "p2p":
+            from kvquant.splitkv import PeerExchange
+            try:
+                pex = PeerExchange(H * G, D, L, device, group)
+            except Exception as e:  # no symmetric memory here: NCCL all-gather + merge
+                err = f"{type(e).__name__}: {e}"
+        agree = torch.tensor([1 if pex is not None else 0], dtype=torch.int32, device=device)
+        dist.all_reduce(agree, op=dist.ReduceOp.MIN)
+        if int(agree.item()) == 0:
+            pex = None
+            if err:
+                print(f"[bench] peer-memory exchange unavailable, using NCCL: {err}", file=sys.stderr)
+        W["pex"] = pex
+        exchange = "p2p (hx_exchange_merge over symmetric memory)" if pex is not None else \
+            "nccl (all_gather_into_tensor + hx_merge_gathered)"
 
     # ---- device-resident timing (CUDA graph replay)
     step = make_step(W, world, group)
@@ -947,7 +980,8 @@ def run_ours(args):
             "dtype": "fp16 values, nuq2/nuq4 codes, fp32 softmax",
             "data": "synthetic (seeded N(0,1) x log-uniform channel scales, x10 outliers; random queries)",
             "config": workload(args, world),
-            "run": {"cuda_graph": use_graph, "n_splits_per_head": W["ns"], "steps_replayed": args.steps},
+            "run": {"cuda_graph": use_graph, "n_splits_per_head": W["ns"], "steps_replayed": args.steps,
+                    "exchange": exchange},
             "roofline": roofline(dom_b, dom_ms, peak, peak_src, dom, read_traffic(dom)),
             "kernels": {"quest_select_ms_per_layer": round(sel_avg, 5), "decode_ms_per_layer": round(dec_avg, 5),
                         "quest_select_GBps": round(sc_b / (sel_avg * 1e-3) / 1e9, 1),

@@ -417,7 +417,6 @@ __global__ void __launch_bounds__(128, 4)
     uint8_t* blk = pool.codes + ((int64_t)h * NB + pg) * seg_bytes + blk_off;
     uint32_t* rec = pool.dir + (((int64_t)h * NB + pg) * 2 + (IS_V ? 1 : 0)) * 4;
     uint16_t* st = pool.stats + ((int64_t)h * NB + pg) * 2 * PF_D + 4 * lane;
-    const bool excl = (__ldcg(rec + 3) & kRunsMask) == kRunsOne;
 
     // ---- one round of asynchronous copies: rows, V threshold rows, record, stats
     __syncwarp();  // the previous run's readers of the buffers are done
@@ -436,12 +435,12 @@ __global__ void __launch_bounds__(128, 4)
         vband = e == 0 ? (uint32_t)sc.v_upper[rr] : (uint32_t)sc.v_lower[rr];
       }
     }
-    if (excl) {
-      if (lane == 0) cp_async_16(ws.rec, rec);
-      if (!IS_V) {
-        cp_async_8(&ws.st[lane][0], st);
-        cp_async_8(&ws.st[lane][2], st + PF_D);
-      }
+    // the record and stats come along whoever owns the page: for a page with
+    // one run in this launch (the pre-pass's count) they are this warp's
+    if (lane == 0) cp_async_16(ws.rec, rec);
+    if (!IS_V) {
+      cp_async_8(&ws.st[lane][0], st);
+      cp_async_8(&ws.st[lane][2], st + PF_D);
     }
     cp_async_commit();
     if (IS_V) {
@@ -450,6 +449,7 @@ __global__ void __launch_bounds__(128, 4)
     }
     cp_async_wait_all();
     __syncwarp();
+    const bool excl = (ws.rec[3] & kRunsMask) == kRunsOne;
 
     uint32_t cmina = 0x001F001Fu, cminb = 0x001F001Fu, cmaxa = 0u, cmaxb = 0u;  // K code range (+1 for max)
     float emin[4], emax[4];  // K outliers and scanned elements, exact values

@@ -73,6 +73,8 @@ _SIGS = {
                                        c_i32, c_vp, c_vp, c_vp, c_vp]),
     "hx_merge_partials": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]),
     "hx_merge_gathered": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "hx_exchange_merge": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp,
+                                  ctypes.c_uint32, c_vp]),
     "hx_selected_attention": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                                       c_i32, c_i32, c_f32, c_vp]),
 }
@@ -109,7 +111,7 @@ def lib():
 LAUNCHES = {"hx_scales_prepare": 2, "hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 1, "hx_unpack_pages": 1,
             "hx_nuq_pack_dense": 1, "hx_nuq_unpack_dense": 1, "hx_nuq_quantize_flat": 2,
             "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": 1, "hx_quest_threshold_slices": 1,
-            "hx_quest_compact": 1, "hx_quest_lists": 2, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_merge_partials": 1, "hx_merge_gathered": 1,
+            "hx_quest_compact": 1, "hx_quest_lists": 2, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_merge_partials": 1, "hx_merge_gathered": 1, "hx_exchange_merge": 1,
             "hx_selected_attention": 1}
 launch_count = [0]
 

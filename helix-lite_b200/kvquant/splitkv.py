@@ -80,6 +80,55 @@ class Exchange:
         return out, self.lse_out
 
 
+class PeerExchange:
+    """The exchange of every layer's partials over peer memory (no NCCL).
+
+    Each rank owns symmetric buffers (torch's symmetric memory: every rank
+    maps every other rank's allocation, CUDA IPC over NVLink): ``rows``
+    (layers, N * (D + 1)) fp32 whose row l the decode of layer l writes
+    ([o | lse], through ``o_view`` / ``lse_view``), and ``flags`` (layers,
+    R) uint32. ``merge(l, out)`` launches hx_exchange_merge: signal, wait
+    for every rank (bounded), merge the R rows read from the peers. One small
+    kernel per layer replaces an all-gather plus the merge kernel, and it
+    captures into a CUDA graph. Raises if symmetric memory is unavailable
+    (callers fall back to ``Exchange``).
+    """
+
+    def __init__(self, N: int, D: int, layers: int, device, group=None, max_polls: int = 1 << 20):
+        import torch.distributed._symmetric_memory as symm
+        self.N, self.D, self.layers = N, D, layers
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        grp = group if group is not None else dist.group.WORLD
+        self.rows = symm.empty((layers, N * (D + 1)), dtype=torch.float32, device=device)
+        self.flags = symm.empty((layers * self.world,), dtype=torch.int32, device=device)
+        self.flags.zero_()
+        h_rows = symm.rendezvous(self.rows, grp)
+        h_flags = symm.rendezvous(self.flags, grp)
+        self.peer_rows = torch.tensor(list(h_rows.buffer_ptrs), dtype=torch.int64, device=device)
+        self.peer_flags = torch.tensor(list(h_flags.buffer_ptrs), dtype=torch.int64, device=device)
+        self.lse_out = torch.empty((layers, N), dtype=torch.float32, device=device)
+        self.max_polls = int(max_polls)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+
+    def o_view(self, layer: int) -> torch.Tensor:
+        return self.rows[layer, :self.N * self.D].view(self.N, self.D)
+
+    def lse_view(self, layer: int) -> torch.Tensor:
+        return self.rows[layer, self.N * self.D:]
+
+    def merge(self, layer: int, out: torch.Tensor, out16: torch.Tensor | None = None):
+        """Exchange and merge layer ``layer`` into ``out`` (N, D) fp32; returns (out, lse)."""
+        import hxlib
+        dev = self.rows.device
+        with torch.cuda.device(dev):
+            hxlib.call("hx_exchange_merge", hxlib.stream(dev), hxlib.ptr(self.peer_rows), hxlib.ptr(self.peer_flags),
+                       self.world, self.rank, layer, self.N, self.D, hxlib.ptr(out), hxlib.ptr(self.lse_out[layer]),
+                       hxlib.ptr(out16), self.max_polls, hxlib.ptr(hxlib.err_word(dev)))
+        return out, self.lse_out[layer]
+
+
 _EXCHANGES: dict = {}
 
 

@@ -349,6 +349,25 @@ HX_API int hx_merge_gathered(void* stream, const float* gathered, int32_t R, int
                              float* lse, uint16_t* out16);
 
 /*
+ * The split-KV exchange and merge of one layer over peer memory (no NCCL):
+ * peer_rows / peer_flags are device arrays of R device pointers (this
+ * process's view of every rank's symmetric buffers, e.g. from CUDA IPC):
+ * rank r's rows (slots, N * (D + 1)) fp32, row `slot` = [o (N x D) | lse (N)]
+ * written by its decode, and its flags (slots, R) uint32, zero at start.
+ * The kernel sets flag (slot, rank) on every rank, waits until all R flags
+ * (slot, *) of its own array are set (at most max_polls polls, then
+ * HX_DEV_ERR_TIMEOUT and nothing merged), merges the R rows read from the
+ * peers into o (N, D), lse (N) (and out16 if non-NULL), then clears its own
+ * (slot, *) flags. Each rank calls it once per slot per step, slots in the
+ * same order on every rank. R <= 32, N <= 64. No reference counterpart (the
+ * reference decodes on one GPU; this replaces an all-gather plus
+ * hx_merge_partials).
+ */
+HX_API int hx_exchange_merge(void* stream, const uint64_t* peer_rows, const uint64_t* peer_flags, int32_t R,
+                             int32_t rank, int32_t slot, int32_t N, int32_t D, float* o, float* lse,
+                             uint16_t* out16, uint32_t max_polls, uint32_t* dev_err);
+
+/*
  * selected_attention on dense pages (quest/reference.py:136-168), fp32
  * arithmetic, grouped-query: q (Hq, D), K / V pages (P, S, H, D) (dtype 0
  * fp32 / 1 fp16), page_idx (k, H) int64 (column h: pages of KV head h).
