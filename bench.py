@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="split-KV exchange: peer-memory merge kernel, or NCCL all-gather + merge")
     ap.add_argument("--profile", action="store_true", help="setup + warmup + steps only (for ncu)")
+    ap.add_argument("--select", choices=["shard", "global"], default="shard",
+                    help="N > 1: top-K per shard (the default), or the single-GPU top-K over every shard's pages")
     return ap.parse_args()
 
 
@@ -248,11 +250,21 @@ def build_world(args, rank, world, device):
     sl = torch.tensor([shard.n_pages * S], dtype=torch.int32, device=device)
     kk = local_k(shard)
     ns = fused.default_splits(1, H, shard.n_pages)
+    gsel = None
+    if args.select == "global" and world > 1:
+        from kvquant.splitkv import GlobalSelect
+        if n_pages % world:
+            raise SystemExit("--select global needs the pages split evenly over the GPUs")
+        gsel = GlobalSelect(1, H, shard.n_pages, world, device, sink_pages=4, top_frac=(1, 4))
+        gsel.set_lengths(torch.tensor([args.ctx], dtype=torch.int32))
 
     # algorithmic bytes: selection is fixed per layer (fixed queries)
     per_layer = []
     for li in range(args.layers):
-        sel = fused.quest_select(pool, li, qs[li], bt, sl, top_k=kk, sink_pages=shard.sink_pages)
+        if gsel is not None:
+            sel = gsel.select(pool, li, qs[li], bt, sl, shard)
+        else:
+            sel = fused.quest_select(pool, li, qs[li], bt, sl, top_k=kk, sink_pages=shard.sink_pages)
         lists, counts = fused.selected_lists(sel)
         lay = pool.layers[li]
         dirc = lay.dir[:, :, :, 2].to(torch.int64)                 # (H, NB, 2)
@@ -274,7 +286,7 @@ def build_world(args, rank, world, device):
         pack_bytes += shard.n_pages * H * lay.seg                        # codes written
         pack_bytes += shard.n_pages * H * 2 * D * 2 * 2                  # stats read + written
         pack_bytes += 4 * int(lay.dir[:, :, :, 2].to(torch.int64).sum())  # outlier entries written
-    return dict(pool=pool, shard=shard, qs=qs, bt=bt, sl=sl, k=kk, ns=ns, per_layer=per_layer,
+    return dict(pool=pool, shard=shard, qs=qs, bt=bt, sl=sl, k=kk, ns=ns, per_layer=per_layer, gsel=gsel,
                 pack=dict(ms=pack_ms, tokens=pack_tokens, bytes=pack_bytes), scales=scales, layout=layout)
 
 
@@ -303,8 +315,11 @@ def make_step(W, world, group, timing=None):
         for li in range(L):
             if timing is not None:
                 timing["ev"][li][0].record()
-            sel = fused.quest_select(pool, li, q_all[li], bt, sl, top_k=W["k"], sink_pages=shard.sink_pages,
-                                     scores=scores[li], thresh=thresh[li], slice_out=slices[li])
+            if W.get("gsel") is not None:
+                sel = W["gsel"].select(pool, li, q_all[li], bt, sl, shard)
+            else:
+                sel = fused.quest_select(pool, li, q_all[li], bt, sl, top_k=W["k"], sink_pages=shard.sink_pages,
+                                         scores=scores[li], thresh=thresh[li], slice_out=slices[li])
             if timing is not None:
                 timing["ev"][li][1].record()
             # one GPU: the decode writes the layer's output in place; several:
@@ -354,8 +369,12 @@ def check_parity(W, args, world, rank, group):
     step = make_step(W, world, group)
     o_all = step().clone()
     torch.cuda.synchronize()
+    gsel = W.get("gsel")
     for li in check_layers:
-        sel = fused.quest_select(pool, li, qs[li], bt, sl, top_k=W["k"], sink_pages=shard.sink_pages, lists=True)
+        if gsel is not None:
+            sel = gsel.select(pool, li, qs[li], bt, sl, shard)
+        else:
+            sel = fused.quest_select(pool, li, qs[li], bt, sl, top_k=W["k"], sink_pages=shard.sink_pages)
         lists, counts = fused.selected_lists(sel)
         scores = sel.scores[0].cpu().numpy()                                   # (H, n)
         lay = pool.layers[li]
@@ -364,6 +383,26 @@ def check_parity(W, args, world, rank, group):
         qp, qn = oq.group_terms(q, G, "sum")
         ref_scores = oq.page_scores(qp, qn, stats[:, :, 0].transpose(1, 0, 2), stats[:, :, 1].transpose(1, 0, 2))
         sel_ok &= bool(np.array_equal(ref_scores.T.view(np.uint32), scores.view(np.uint32)))
+        full = None
+        if world > 1:   # every rank's oracle scores, in global page order
+            dev = pool.device
+            sizes = torch.tensor([n], device=dev)
+            all_n = [torch.empty_like(sizes) for _ in range(world)]
+            dist.all_gather(all_n, sizes, group=group)
+            nmax = max(int(x) for x in all_n)
+            pad = torch.full((H, nmax), float("nan"), device=dev)
+            pad[:, :n] = torch.from_numpy(np.ascontiguousarray(ref_scores.T)).to(dev)
+            all_sc = [torch.empty_like(pad) for _ in range(world)]
+            dist.all_gather(all_sc, pad, group=group)
+            full = np.concatenate([all_sc[r][:, :int(all_n[r])].cpu().numpy() for r in range(world)], axis=1)
+
+        def expected(h):
+            if gsel is None:
+                return oq.select_pages(ref_scores[:, h], W["k"], shard.sink_pages)
+            g_sel = oq.select_pages(full[h], full.shape[1] // 4, 4)      # the one-GPU selection
+            mine = g_sel[(g_sel >= shard.page_begin) & (g_sel < shard.page_begin + n)]
+            return mine - shard.page_begin
+
         codes = lay.codes.cpu().numpy()
         rbk, rbv = D * lay.bits_k // 8, D * lay.bits_v // 8
         arena = lay.arena.cpu().numpy()
@@ -374,9 +413,11 @@ def check_parity(W, args, world, rank, group):
         o_part = np.zeros((H * G, D))
         lse_part = np.full(H * G, -np.inf)
         for h in range(H):
-            pages = oq.select_pages(ref_scores[:, h], W["k"], shard.sink_pages)
+            pages = expected(h)
             c = int(counts[0, h])
             sel_ok &= bool(np.array_equal(lists[0, h, :c].cpu().numpy(), pages))
+            if len(pages) == 0:
+                continue
             kr = codes[h, :, :S * rbk].reshape(n, S, rbk)
             vr = codes[h, :, S * rbk:].reshape(n, S, rbv)
             Kd, Vd = dequant_packed_pages(kr, vr, dirs[h], arena, pages, (shard.page_begin + pages) * S,
@@ -393,15 +434,6 @@ def check_parity(W, args, world, rank, group):
             t = torch.from_numpy(np.concatenate([o_part.reshape(-1), lse_part])).to(dev)
             got = [torch.empty_like(t) for _ in range(world)]
             dist.all_gather(got, t, group=group)
-            sc_t = torch.from_numpy(np.ascontiguousarray(scores)).to(dev)
-            sizes = torch.tensor([n], device=dev)
-            all_n = [torch.empty_like(sizes) for _ in range(world)]
-            dist.all_gather(all_n, sizes, group=group)
-            nmax = max(int(x) for x in all_n)
-            pad = torch.full((H, nmax), float("nan"), device=dev)
-            pad[:, :n] = sc_t
-            all_sc = [torch.empty_like(pad) for _ in range(world)]
-            dist.all_gather(all_sc, pad, group=group)
             sel_t = torch.tensor([1 if sel_ok else 0], device=dev)
             dist.all_reduce(sel_t, op=dist.ReduceOp.MIN)
             sel_ok = bool(sel_t.item())
@@ -411,7 +443,6 @@ def check_parity(W, args, world, rank, group):
                 L_ = np.stack([p[H * G * D:] for p in parts])
                 ref_o, _ = oatt.merge_partials(O, L_)
                 errs.append(float(np.abs(o_all[li].cpu().numpy() - ref_o).max()))
-                full = np.concatenate([all_sc[r][:, :int(all_n[r])].cpu().numpy() for r in range(world)], axis=1)
                 nt = full.shape[1]
                 from kvquant.splitkv import shard_plan
                 hit = tot = 0
@@ -420,8 +451,12 @@ def check_parity(W, args, world, rank, group):
                     mine = set()
                     for r in range(world):
                         srd = shard_plan(nt, world, r)
-                        loc = oq.select_pages(full[h, srd.page_begin:srd.page_begin + srd.n_pages],
-                                              srd.n_pages // 4, srd.sink_pages)
+                        if gsel is not None:
+                            loc = np.asarray(sorted(p for p in glob if srd.page_begin <= p < srd.page_begin
+                                                    + srd.n_pages), dtype=np.int64) - srd.page_begin
+                        else:
+                            loc = oq.select_pages(full[h, srd.page_begin:srd.page_begin + srd.n_pages],
+                                                  srd.n_pages // 4, srd.sink_pages)
                         mine |= set((loc + srd.page_begin).tolist())
                     hit += len(glob & mine)
                     tot += len(glob)
@@ -430,9 +465,11 @@ def check_parity(W, args, world, rank, group):
             errs.append(float(np.abs(o_all[li].cpu().numpy() - o_part).max()))
     if rank != 0:
         return None
+    how = ("the one-GPU top-K over every rank's pages (oracle scores gathered), each rank's part"
+           if gsel is not None else "pinned scores + top-K on each rank's pages")
     res = {"layers": check_layers, "selection_bit_exact": sel_ok, "decode_max_abs_err": max(errs), "tol": TOL,
-           "reference": "oracle: pinned scores + top-K on each rank's pages; float64 attention over the "
-                        "oracle's decode of the pool bytes" + ("; exact partials merged" if world > 1 else ""),
+           "reference": "oracle: " + how + "; float64 attention over the oracle's decode of the pool bytes"
+                        + ("; exact partials merged" if world > 1 else ""),
            "ok": bool(sel_ok and max(errs) < TOL)}
     if world > 1:
         res["page_recall_vs_global_topk"] = round(min(recall), 4)
@@ -981,7 +1018,9 @@ def run_ours(args):
             "data": "synthetic (seeded N(0,1) x log-uniform channel scales, x10 outliers; random queries)",
             "config": workload(args, world),
             "run": {"cuda_graph": use_graph, "n_splits_per_head": W["ns"], "steps_replayed": args.steps,
-                    "exchange": exchange},
+                    "exchange": exchange,
+                    "selection": ("top-K of the whole sequence (one GPU's)" if world == 1 or W.get("gsel") is not None
+                                  else "top-K of each shard's pages")},
             "roofline": roofline(dom_b, dom_ms, peak, peak_src, dom, read_traffic(dom)),
             "kernels": {"quest_select_ms_per_layer": round(sel_avg, 5), "decode_ms_per_layer": round(dec_avg, 5),
                         "quest_select_GBps": round(sc_b / (sel_avg * 1e-3) / 1e9, 1),

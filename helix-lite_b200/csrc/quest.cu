@@ -907,6 +907,201 @@ __global__ void __launch_bounds__(256) quest_threshold_kernel(const float* __res
 }
 
 // ---------------------------------------------------------------------------
+// exact threshold, one CTA per (b, h): for short rows (batched sequences)
+// one block reads the whole row, so the boundary bin's candidates, the
+// level-2 counts and the slice counts stay in shared memory and nothing waits
+// on other blocks (no candidate reservation, fence or last-block counter).
+// Same thresholds and slice counts as quest_threshold_kernel. Measured on
+// B200 (with the histogram kernel): 8.7 us against 9.9 us for the sliced
+// kernel at 2048 pages, but 16.6 against 11.7 us at 8192 pages, where one
+// block's serial rounds over the row outweigh the saved round trips.
+
+constexpr int kRowCand = 2048;      // boundary-bin candidates kept in smem
+constexpr int kRowMaxPages = 2048;  // longer rows take the sliced kernel
+
+// Count the warp's taken pages into their slices. Lanes hold consecutive
+// pages (slice s >= 0; s < 0 and take false past the row's end), so when
+// lanes 0 and 31 share a slice every lane does: one add for the warp.
+// Otherwise (a slice edge or the row's tail) each taken lane adds its own.
+HX_DEVINL void slice_add(uint32_t* s_add, int s, bool take) {
+  const uint32_t taken = __ballot_sync(0xffffffffu, take);
+  const int s0 = __shfl_sync(0xffffffffu, s, 0), s31 = __shfl_sync(0xffffffffu, s, 31);
+  if (s0 == s31) {
+    if (taken && lane_id() == 0) atomicAdd(&s_add[s0], (uint32_t)__popc(taken));
+  } else if (take) {
+    atomicAdd(&s_add[s], 1u);
+  }
+}
+
+__global__ void __launch_bounds__(256) quest_threshold_row_kernel(
+    const float* __restrict__ scores, int H, const int32_t* __restrict__ seq_lens, int S, int max_pages,
+    int sinks_req, int k_fixed, int fnum, int fden, int C, uint32_t* hist, uint64_t* cand, uint64_t* thresh,
+    int32_t* slice_off, uint32_t* err) {
+  __shared__ __align__(16) uint32_t s_hist[kBins];  // level 1, then level 2, then the level-2 bin's keys
+  __shared__ uint64_t s_cand[kRowCand];
+  __shared__ uint32_t s_warp[8];
+  __shared__ int s_res[4];
+  __shared__ uint32_t s_h2[256];
+  __shared__ uint32_t s_add[kMaxSlices];
+  __shared__ uint32_t s_nc;
+  pdl_allow_next();
+  pdl_wait();  // the scores and the level-1 histogram come from the scoring kernel
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x;
+  const SelPlan pl = plan_for(seq_lens[bh / H], S, max_pages, sinks_req, k_fixed, fnum, fden);
+  uint32_t* hist_bh = hist + (int64_t)bh * 2 * kBins;
+  uint64_t* cand_bh = cand + (int64_t)bh * max_pages;
+  const float* sc = scores + (int64_t)bh * max_pages;
+  const int n_ns = pl.n - pl.sinks;
+  const int per = n_ns > 0 ? (n_ns + C - 1) / C : 1;
+  const bool trivial = pl.k_eff == 0 || pl.k_eff >= n_ns;
+  for (int i = tid; i < C; i += blockDim.x)
+    s_add[i] = (trivial && pl.k_eff > 0) ? (uint32_t)max(0, min(per, n_ns - i * per)) : 0u;
+  if (tid == 0) s_nc = 0;
+
+  uint64_t T = pl.k_eff == 0 ? ~0ull : 0ull;
+  if (!trivial) {
+    const uint32_t anchor = order_key(sc[pl.sinks]);
+    load_hist(s_hist, hist_bh);
+    __syncthreads();
+    uint32_t above;
+    const int bstar = find_boundary(s_hist, (uint32_t)pl.k_eff, above, s_warp, s_res);
+    if (bstar < 0) {
+      if (tid == 0) set_err(err, HX_DEV_ERR_SELECT);
+    } else {
+      const uint32_t r = (uint32_t)pl.k_eff - above;
+      const bool full_bin = s_hist[bstar] == r;
+      const bool split2 = !full_bin && !edge_bin(bstar);
+      __syncthreads();  // level 1 read: its smem becomes the level-2 counts
+      for (int i = tid; i < kBins; i += blockDim.x) s_hist[i] = 0;
+      __syncthreads();
+      // the row: pages above the boundary bin go to their slice's count;
+      // the bin's pages become candidates (every one in global memory, the
+      // first kRowCand also in smem) with their level-2 counts
+      constexpr int kRowU = 8;  // loads in flight per thread
+      for (int base = pl.sinks; base < pl.n; base += kRowU * (int)blockDim.x) {
+        float v[kRowU];
+#pragma unroll
+        for (int u = 0; u < kRowU; ++u) {  // loads first, so they are in flight together
+          const int j = base + u * (int)blockDim.x + tid;
+          v[u] = j < pl.n ? __ldg(sc + j) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kRowU; ++u) {
+          const int j = base + u * (int)blockDim.x + tid;
+          const bool valid = j < pl.n;
+          const uint32_t k32 = order_key(v[u]);
+          const int b1 = valid ? bin1(k32, anchor) : -1;
+          slice_add(s_add, valid ? (j - pl.sinks) / per : -1, b1 > bstar || (full_bin && b1 == bstar));
+          if (b1 == bstar && !full_bin) {
+            const uint64_t key = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
+            const uint32_t at = atomicAdd(&s_nc, 1u);
+            cand_bh[at] = key;
+            if (at < (uint32_t)kRowCand) s_cand[at] = key;
+            if (split2) atomicAdd(&s_hist[bin2(k32, anchor)], 1u);
+          }
+        }
+      }
+      __syncthreads();
+      const uint32_t cnt = s_nc;
+      const bool in_smem = cnt <= (uint32_t)kRowCand;
+      if (full_bin) {
+        T = bin_floor(bstar, -1, anchor);
+      } else if (!split2) {
+        T = in_smem ? radix_select<false>(s_cand, cnt, r, 0ull, 64, s_h2, s_warp, s_res)
+                    : radix_select<true>(cand_bh, cnt, r, 0ull, 64, s_h2, s_warp, s_res);
+      } else {
+        uint32_t above2;
+        const int b2 = find_boundary(s_hist, r, above2, s_warp, s_res);
+        if (b2 < 0) {
+          T = bin_floor(bstar, -1, anchor);
+          if (tid == 0) set_err(err, HX_DEV_ERR_SELECT);
+        } else {
+          const uint32_t r2 = r - above2;
+          if (s_hist[b2] == r2) {
+            T = bin_floor(bstar, b2, anchor);
+          } else {
+            // the level-2 bin's keys (the counts' smem is free now), ranked
+            uint64_t* hand = reinterpret_cast<uint64_t*>(s_hist);
+            constexpr uint32_t kHand = kBins / 2;
+            __syncthreads();
+            if (tid == 0) s_nc = 0;
+            __syncthreads();
+            for (uint32_t i = tid; i < cnt; i += blockDim.x) {
+              const uint64_t key = in_smem ? s_cand[i] : __ldcg(cand_bh + i);
+              if (bin2((uint32_t)(key >> 32), anchor) == b2) {
+                const uint32_t at = atomicAdd(&s_nc, 1u);
+                if (at < kHand) hand[at] = key;
+              }
+            }
+            __syncthreads();
+            const uint32_t nc = s_nc;
+            if (nc <= blockDim.x) {
+              // a handful of keys: key i is T when exactly r2 - 1 keys beat it
+              if (tid == 0) s_res[0] = -1;
+              __syncthreads();
+              if ((uint32_t)tid < nc) {
+                const uint64_t mine = hand[tid];
+                uint32_t beat = 0;
+                for (uint32_t i = 0; i < nc; ++i) beat += hand[i] > mine;
+                if (beat + 1 == r2) s_res[0] = tid;
+              }
+              __syncthreads();
+              const int w = s_res[0];
+              T = w >= 0 ? hand[w] : bin_floor(bstar, b2, anchor);
+              if (w < 0 && tid == 0) set_err(err, HX_DEV_ERR_SELECT);
+            } else if (nc <= kHand) {
+              T = radix_select<false>(hand, nc, r2, 0ull, 64, s_h2, s_warp, s_res);
+            } else {
+              T = in_smem ? radix_select<false>(s_cand, cnt, r, 0ull, 64, s_h2, s_warp, s_res)
+                          : radix_select<true>(cand_bh, cnt, r, 0ull, 64, s_h2, s_warp, s_res);
+            }
+          }
+        }
+      }
+      // the candidates that pass join their slices' counts
+      __syncthreads();
+      if (slice_off && !full_bin) {
+        for (uint32_t i = tid; i < cnt; i += blockDim.x) {
+          const uint64_t key = in_smem ? s_cand[i] : __ldcg(cand_bh + i);
+          if (key >= T) atomicAdd(&s_add[min(((int)(~(uint32_t)key) - pl.sinks) / per, C - 1)], 1u);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (slice_off && tid < 32) {  // exclusive prefix of the slice counts (one warp)
+    const int lane = tid;
+    uint32_t v[kMaxSlices / 32];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int q = 0; q < kMaxSlices / 32; ++q) {
+      const int i = (kMaxSlices / 32) * lane + q;
+      v[q] = i < C ? s_add[i] : 0u;
+      sum += v[q];
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += x;
+    }
+    uint32_t acc = incl - sum;
+#pragma unroll
+    for (int q = 0; q < kMaxSlices / 32; ++q) {
+      const int i = (kMaxSlices / 32) * lane + q;
+      if (i < C) slice_off[(int64_t)bh * (C + 1) + i] = (int32_t)acc;
+      acc += v[q];
+    }
+    if (lane == 31) slice_off[(int64_t)bh * (C + 1) + C] = (int32_t)incl;
+  }
+  if (tid == 0) thresh[bh] = T;
+  // leave the level-1 counts zero for the next scoring (the scoring kernel
+  // counts every row, trivial or not; level 2 lives in smem here)
+  for (int i = tid; i < kBins; i += blockDim.x) hist_bh[i] = 0;
+}
+
+// ---------------------------------------------------------------------------
 // compaction to ascending page lists (API output; the decode reads thresholds)
 
 HX_DEVINL bool page_selected(const float* scores_bh, uint64_t T, int j, int sinks) {
@@ -1058,6 +1253,82 @@ __global__ void __launch_bounds__(kListThreads) quest_list_scatter_kernel(
   if (c == nch - 1 && threadIdx.x == kListThreads - 1) counts[row] = min(pos, max_out);
 }
 
+// ---------------------------------------------------------------------------
+// global top-K over split-KV shards
+//
+// A threshold T over the whole sequence's pages (global page indices: the key
+// of page g is order_key(score) << 32 | ~g) selects, among pages whose score
+// key equals T's high word kT, those with g <= ~low(T). On a shard whose page
+// 0 is global page `base`, the same pages are local pages j = g - base with
+// key order_key(score) << 32 | ~j, so the shard's threshold keeps kT and
+// moves the index bound down by `base`; when the bound lies before the shard
+// none of its ties are taken (threshold kT + 1). 0 (every page) and ~0 (no
+// page) need no change, and no score key reaches 0xFFFFFFFF, so a threshold
+// with that high word selects nothing anywhere.
+HX_DEVINL uint64_t shard_threshold(uint64_t Tg, uint32_t base) {
+  if (Tg == 0ull || Tg == ~0ull) return Tg;
+  const uint32_t kT = (uint32_t)(Tg >> 32);
+  if (kT == 0xFFFFFFFFu) return Tg;
+  const uint32_t gmax = ~(uint32_t)Tg;  // last global index of the ties taken
+  if (gmax < base) return (uint64_t)(kT + 1u) << 32;
+  return ((uint64_t)kT << 32) | (uint64_t)(~(gmax - base));
+}
+
+// One block per (b, h): this shard's threshold and the decode's slice counts
+// of its local pages (the slices of hx_quest_threshold_slices: C slices of
+// ceil((n - sinks) / C) non-sink pages, exclusive prefix of the selected
+// counts, total in entry C).
+__global__ void __launch_bounds__(1024) quest_localize_kernel(const uint64_t* __restrict__ thresh_g, int H,
+                                                             const int32_t* __restrict__ seq_lens, int S,
+                                                             int max_pages, int sinks_req, int page_begin,
+                                                             const float* __restrict__ scores, int C,
+                                                             uint64_t* __restrict__ thresh,
+                                                             int32_t* __restrict__ slice_off) {
+  __shared__ uint32_t s_cnt[kMaxSlices];
+  const int bh = blockIdx.x;
+  const int lane = lane_id();
+  const int n = min((seq_lens[bh / H] + S - 1) / S, max_pages);
+  const int sinks = min(max(sinks_req, 0), n);
+  const uint64_t T = shard_threshold(thresh_g[bh], (uint32_t)page_begin);
+  for (int i = threadIdx.x; i < C; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+  const int n_ns = n - sinks;
+  const int per = n_ns > 0 ? (n_ns + C - 1) / C : 1;
+  const float* sc = scores + (int64_t)bh * max_pages;
+  // a warp takes 32 consecutive pages per round (slice_add)
+  for (int j0 = sinks + (threadIdx.x & ~31); j0 < n; j0 += blockDim.x) {
+    const int j = j0 + lane;
+    const bool sel = j < n && order_key64(__ldg(sc + j), (uint32_t)j) >= T;
+    slice_add(s_cnt, j < n ? (j - sinks) / per : -1, sel);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    uint32_t v[kMaxSlices / 32];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int q = 0; q < kMaxSlices / 32; ++q) {
+      const int i = (kMaxSlices / 32) * lane + q;
+      v[q] = i < C ? s_cnt[i] : 0u;
+      sum += v[q];
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += x;
+    }
+    uint32_t acc = incl - sum;
+#pragma unroll
+    for (int q = 0; q < kMaxSlices / 32; ++q) {
+      const int i = (kMaxSlices / 32) * lane + q;
+      if (i < C) slice_off[(int64_t)bh * (C + 1) + i] = (int32_t)acc;
+      acc += v[q];
+    }
+    if (lane == 31) slice_off[(int64_t)bh * (C + 1) + C] = (int32_t)incl;
+  }
+  if (threadIdx.x == 0) thresh[bh] = T;
+}
+
 }  // namespace hx
 
 // ===========================================================================
@@ -1178,6 +1449,15 @@ HX_API int hx_quest_threshold_slices(void* stream, const float* scores, int32_t 
     if (hg.x == 0) hg.x = 1;
     quest_hist_kernel<<<hg, 256, 0, st>>>(scores, H, seq_lens, page_size, max_pages, sink_pages, hist);
   }
+  if (max_pages <= kRowMaxPages) {
+    if (hx_launch_pdl(quest_threshold_row_kernel, dim3(B * H), dim3(256), 0, st, scores, (int)H, seq_lens,
+                      (int)page_size, (int)max_pages, (int)sink_pages, (int)k_fixed, (int)frac_num, (int)frac_den,
+                      quest_slices(max_pages), hist, cand, thresh, slice_off, dev_err) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return HX_ERR_LAUNCH;
+    }
+    return HX_OK;
+  }
   dim3 grid(quest_slices(max_pages), B * H);
   if (hx_launch_pdl(quest_threshold_kernel, grid, dim3(256), 0, st, scores, (int)H, seq_lens, (int)page_size,
                     (int)max_pages, (int)sink_pages, (int)k_fixed, (int)frac_num, (int)frac_den, hist, cand, counters,
@@ -1219,6 +1499,20 @@ HX_API int hx_quest_lists(void* stream, const float* scores, const uint64_t* thr
   quest_list_scatter_kernel<<<grid, kListThreads, 0, S_(stream)>>>(scores, thresh, H, seq_lens, page_size,
                                                                    max_pages, sink_pages, nch, chunk_counts,
                                                                    max_out, out, counts);
+  HX_LAUNCH_CHECK();
+  return HX_OK;
+}
+
+HX_API int hx_quest_localize(void* stream, const uint64_t* thresh_global, const float* scores, int32_t B,
+                             int32_t H, const int32_t* seq_lens, int32_t page_size, int32_t max_pages,
+                             int32_t sink_pages, int32_t page_begin, uint64_t* thresh, int32_t* slice_off) {
+  if (B < 0 || H <= 0 || page_size <= 0 || max_pages < 0 || page_begin < 0) return HX_ERR_ARG;
+  if (B == 0) return HX_OK;
+  if (!thresh_global || !scores || !seq_lens || !thresh || !slice_off) return HX_ERR_ARG;
+  if ((int64_t)B * H > 2147483647ll) return HX_ERR_UNSUPPORTED;
+  quest_localize_kernel<<<B * H, 1024, 0, S_(stream)>>>(thresh_global, H, seq_lens, page_size, max_pages,
+                                                        sink_pages, page_begin, scores, quest_slices(max_pages),
+                                                        thresh, slice_off);
   HX_LAUNCH_CHECK();
   return HX_OK;
 }

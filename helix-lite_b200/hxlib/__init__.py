@@ -64,6 +64,7 @@ _SIGS = {
     "hx_quest_compact": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32,
                                  c_vp, c_vp]),
     "hx_quest_lists": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "hx_quest_localize": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]),
     "hx_decode_scratch_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "hx_decode_attn": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_i32, c_i32, c_f32, c_vp, c_i32,
                                c_vp, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_vp, c_i32, c_vp, c_i32,
@@ -108,16 +109,18 @@ def lib():
 
 
 # kernel launches each entry point makes (bench.py counts launches with this)
-LAUNCHES = {"hx_scales_prepare": 2, "hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 1, "hx_unpack_pages": 1,
+LAUNCHES = {"hx_scales_prepare": 2, "hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 3, "hx_unpack_pages": 1,
             "hx_nuq_pack_dense": 1, "hx_nuq_unpack_dense": 1, "hx_nuq_quantize_flat": 2,
-            "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": 1, "hx_quest_threshold_slices": 1,
+            "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": lambda a: 1 if a[11] else 2,
+            "hx_quest_threshold_slices": lambda a: 1 if a[11] else 2, "hx_quest_localize": 1,
             "hx_quest_compact": 1, "hx_quest_lists": 2, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_merge_partials": 1, "hx_merge_gathered": 1, "hx_exchange_merge": 1,
             "hx_selected_attention": 1}
 launch_count = [0]
 
 
 def call(name, *args):
-    launch_count[0] += LAUNCHES.get(name, 0)
+    n = LAUNCHES.get(name, 0)
+    launch_count[0] += n(args) if callable(n) else n
     rc = getattr(lib(), name)(*args)
     if rc != HX_OK:
         what = {HX_ERR_ARG: "invalid argument", HX_ERR_UNSUPPORTED: "unsupported configuration",

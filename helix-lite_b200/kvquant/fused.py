@@ -53,6 +53,22 @@ def _i32(t, device):
     return t.to(device=device, dtype=torch.int32).contiguous()
 
 
+def page_scores(pool: CompactKVPool, layer_idx: int, q: torch.Tensor, bt: torch.Tensor, sl: torch.Tensor,
+                max_pages: int, sink_pages: int, scores: torch.Tensor, hist: torch.Tensor | None = None,
+                gqa: str = "sum"):
+    """Quest bounds of every page of each sequence into ``scores`` (B, H,
+    max_pages) fp32 (one kernel); with ``hist`` also the level-1 key histogram
+    the threshold kernel starts from. q (B, Hq, D) fp16 and bt / sl int32 on
+    the pool's device."""
+    B, Hq, D = q.shape
+    H = pool.num_kv_heads
+    stats = pool.layers[layer_idx].stats
+    call("hx_quest_scores", stream(pool.device), ptr(q), B, H, Hq // H, D, 0 if gqa == "sum" else 1, 1,
+         ptr(stats), hxlib.ctypes.c_void_p(stats.data_ptr() + 2 * D), 2 * D, pool.num_blocks * 2 * D,
+         ptr(bt), bt.shape[1], ptr(sl), pool.block_size, max_pages, sink_pages, ptr(scores),
+         ptr(hist) if hist is not None else None)
+
+
 def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
                  seq_lens: torch.Tensor, *, top_k: int | None = None, top_frac=(1, 4), sink_pages: int = 4,
                  gqa: str = "sum", max_pages: int | None = None, scores: torch.Tensor | None = None,
@@ -83,7 +99,6 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
     bt = _i32(block_table, dev)
     sl = _i32(seq_lens, dev)
     mp = int(max_pages if max_pages is not None else bt.shape[1])
-    lay = pool.layers[layer_idx]
     if scores is None:
         scores = torch.empty((B, H, max(mp, 1)), dtype=torch.float32, device=dev)
     if thresh is None:
@@ -91,12 +106,9 @@ def quest_select(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block
     hist = hxlib.scratch(dev, "quest_hist", B * H * 2 * 4096 * 4)
     cand = hxlib.scratch(dev, "quest_cand", B * H * max(mp, 1) * 8)
     ctr = hxlib.scratch(dev, "quest_ctr", B * H * 2 * 4)
-    stats = lay.stats
     with torch.cuda.device(dev):
         st = stream(dev)
-        call("hx_quest_scores", st, ptr(q), B, H, Hq // H, D, 0 if gqa == "sum" else 1, 1,
-             ptr(stats), hxlib.ctypes.c_void_p(stats.data_ptr() + 2 * D), 2 * D, pool.num_blocks * 2 * D,
-             ptr(bt), bt.shape[1], ptr(sl), S, mp, sink_pages, ptr(scores), ptr(hist))
+        page_scores(pool, layer_idx, q, bt, sl, mp, sink_pages, scores, hist, gqa)
         kf, fn, fd = (int(top_k), 0, 0) if top_k is not None else (0, int(top_frac[0]), int(top_frac[1]))
         nsl = int(hxlib.lib().hx_quest_slices(mp))
         if slice_out is None:

@@ -129,6 +129,88 @@ class PeerExchange:
         return out, self.lse_out[layer]
 
 
+def gather_score_rows(loc: torch.Tensor, gathered: torch.Tensor, glob: torch.Tensor, group=None):
+    """Every rank's page scores in global page order.
+
+    loc (B, H, n) this rank's scores of its n pages; gathered (R, B*H, n)
+    scratch; glob (B, H, R*n) receives row (b, h) = the R ranks' rows (b, h)
+    one after another (rank r's pages are global pages r*n .. r*n + n - 1).
+    One all-gather and one strided copy."""
+    B, H, n = loc.shape
+    R = gathered.shape[0]
+    dist.all_gather_into_tensor(gathered.view(-1), loc.reshape(-1), group=group)
+    glob.view(B * H, R, n).copy_(gathered.permute(1, 0, 2))
+    return glob
+
+
+class GlobalSelect:
+    """Quest selection over the whole sequence when its pages are split.
+
+    With per-shard selection every rank keeps the top quarter of its own
+    pages, which is not the single-GPU top-K. Here each rank scores its own
+    pages, the scores are all-gathered into global page order (R * n fp32
+    per (b, h): 128 KB per rank per layer at 1M tokens on 8 ranks), every
+    rank runs the same exact threshold kernel over the global rows (so the
+    threshold is the single-GPU one, bit for bit, and the ranks agree), and
+    hx_quest_localize turns it into the rank's threshold over its local
+    page indices plus the decode's slice counts. The result is a
+    ``Selection`` the decode takes as usual. Requires equal shards (n pages
+    on every rank; the sequence ends on the last rank). Follows the
+    single-GPU selection of src/kvquant/quest_selector.py:70-83.
+    """
+
+    def __init__(self, B: int, H: int, n_local: int, world: int, device, group=None, sink_pages: int = 4,
+                 top_frac=(1, 4), top_k: int | None = None):
+        import hxlib
+        self.B, self.H, self.n, self.world, self.group = B, H, n_local, world, group
+        self.sinks = sink_pages
+        self.kf, self.fn, self.fd = ((int(top_k), 0, 0) if top_k is not None
+                                     else (0, int(top_frac[0]), int(top_frac[1])))
+        ng = world * n_local
+        f32 = dict(dtype=torch.float32, device=device)
+        self.loc = torch.empty((B, H, n_local), **f32)
+        self.gathered = torch.empty((world, B * H, n_local), **f32)
+        self.glob = torch.empty((B, H, ng), **f32)
+        self.thresh_g = torch.empty((B * H,), dtype=torch.int64, device=device)
+        self.thresh = torch.empty((B * H,), dtype=torch.int64, device=device)
+        self.slice_off = torch.empty((B * H, int(hxlib.lib().hx_quest_slices(n_local)) + 1), dtype=torch.int32,
+                                     device=device)
+        # threshold scratch: left zeroed by the kernel after each use
+        self.hist = torch.zeros((B * H * 2 * 4096,), dtype=torch.int32, device=device)
+        self.cand = torch.empty((B * H * max(ng, 1),), dtype=torch.int64, device=device)
+        self.ctr = torch.zeros((B * H * 2,), dtype=torch.int32, device=device)
+        self.seq_glob = torch.empty((B,), dtype=torch.int32, device=device)
+
+    def set_lengths(self, seq_lens_global: torch.Tensor):
+        """Tokens of each whole sequence (B,); call before capture or when they change."""
+        self.seq_glob.copy_(seq_lens_global.to(self.seq_glob.device, torch.int32))
+
+    def select(self, pool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
+               seq_lens: torch.Tensor, shard: Shard, gqa: str = "sum"):
+        """This rank's part of the global selection: a Selection over its
+        local pages (block_table / seq_lens local, as for splitkv_decode)."""
+        import hxlib
+        from .fused import Selection, page_scores
+        dev = pool.device
+        q = query.to(device=dev, dtype=torch.float16).contiguous()
+        bt = block_table.to(device=dev, dtype=torch.int32).contiguous()
+        sl = seq_lens.to(device=dev, dtype=torch.int32).contiguous()
+        S = pool.block_size
+        sinks = max(0, min(self.sinks - shard.page_begin, self.n))   # the global sinks on this shard
+        with torch.cuda.device(dev):
+            st = hxlib.stream(dev)
+            page_scores(pool, layer_idx, q, bt, sl, self.n, sinks, self.loc, None, gqa)
+            gather_score_rows(self.loc, self.gathered, self.glob, self.group)
+            hxlib.call("hx_quest_threshold_slices", st, hxlib.ptr(self.glob), self.B, self.H, hxlib.ptr(self.seq_glob),
+                       S, self.world * self.n, self.sinks, self.kf, self.fn, self.fd, 0, hxlib.ptr(self.hist),
+                       hxlib.ptr(self.cand), hxlib.ptr(self.ctr), hxlib.ptr(self.thresh_g), None,
+                       hxlib.ptr(hxlib.err_word(dev)))
+            hxlib.call("hx_quest_localize", st, hxlib.ptr(self.thresh_g), hxlib.ptr(self.loc), self.B, self.H,
+                       hxlib.ptr(sl), S, self.n, sinks, shard.page_begin, hxlib.ptr(self.thresh),
+                       hxlib.ptr(self.slice_off))
+        return Selection(self.loc, self.thresh, sl, S, self.n, sinks, None, None, self.slice_off)
+
+
 _EXCHANGES: dict = {}
 
 

@@ -219,7 +219,9 @@ HX_API int hx_quest_scores(void* stream, const uint16_t* q, int32_t B, int32_t H
  * order_key(score) << 32 | ~j; thresh = ~0 when k_eff == 0.
  * Scratch: hist as above (filled by hx_quest_scores when hist_ready != 0,
  * else counted here from `scores`); cand (B*H*max_pages) u64; counters
- * (B*H*2) u32; all zero on entry and left zero. Replaces the torch.topk of
+ * (B*H*2) u32; all zero on entry and left zero. Rows of up to 2048 pages
+ * (max_pages) are resolved by one CTA each; longer ones by one CTA per 1024
+ * pages, the last of them finishing the row. Replaces the torch.topk of
  * topk_pages_with_sinks (reference.py:96-133) with a deterministic order.
  */
 HX_API int hx_quest_threshold(void* stream, const float* scores, int32_t B, int32_t H,
@@ -262,6 +264,23 @@ HX_API int hx_quest_lists(void* stream, const float* scores, const uint64_t* thr
                           int32_t B, int32_t H, const int32_t* seq_lens, int32_t page_size,
                           int32_t max_pages, int32_t sink_pages, int32_t max_out,
                           int32_t* out, int32_t* counts, int32_t* chunk_counts);
+
+/* Global top-K over split-KV shards. thresh_global (B*H) holds thresholds
+ * that hx_quest_threshold computed over the whole sequence's scores (every
+ * shard's pages, in global page order); this shard's pages are global pages
+ * page_begin .. page_begin + max_pages - 1 and its scores (B, H, max_pages)
+ * are indexed locally. Writes the shard's own thresholds (thresh, B*H), which
+ * select with local indices exactly the global selection's pages in this
+ * shard (score ties broken by the global index), and the decode's slice
+ * counts (slice_off (B*H, hx_quest_slices(max_pages) + 1), as
+ * hx_quest_threshold_slices writes them). sink_pages: the global sinks that
+ * fall on this shard, max(0, min(sinks - page_begin, max_pages)). One kernel. The
+ * reference selects on one GPU only (src/kvquant/quest_selector.py:70-83);
+ * this keeps that selection bit for bit when the pages are split. */
+HX_API int hx_quest_localize(void* stream, const uint64_t* thresh_global, const float* scores,
+                             int32_t B, int32_t H, const int32_t* seq_lens, int32_t page_size,
+                             int32_t max_pages, int32_t sink_pages, int32_t page_begin,
+                             uint64_t* thresh, int32_t* slice_off);
 
 /* ---- fused-dequant decode attention (Kernel C) ------------------------ */
 

@@ -138,3 +138,73 @@ def shard_bounds(n_pages: int, n_ranks: int):
     for r in range(n_ranks):
         b.append(b[-1] + base + (1 if r < rem else 0))
     return b
+
+
+def keys64(scores_1d, first_page: int = 0):
+    """64-bit page keys: order key << 32 | ~(global page index); larger = better."""
+    k = order_keys(scores_1d).astype(np.uint64) << np.uint64(32)
+    idx = (np.arange(len(scores_1d), dtype=np.int64) + first_page).astype(np.uint64)
+    return k | (~idx & np.uint64(0xFFFFFFFF))
+
+
+def threshold64(scores_1d, k: int, sink_pages: int) -> int:
+    """The selection as one 64-bit threshold over the non-sink pages' keys:
+    a page is chosen iff its key >= T (0: every page, 2^64-1: none)."""
+    s = np.asarray(scores_1d)
+    n = len(s)
+    sinks = max(0, min(sink_pages, n))
+    k_eff = max(0, min(k, n - sinks))
+    if k_eff == 0:
+        return (1 << 64) - 1
+    if k_eff >= n - sinks:
+        return 0
+    keys = np.sort(keys64(s)[sinks:])[::-1]
+    return int(keys[k_eff - 1])
+
+
+def shard_threshold(T: int, base: int) -> int:
+    """A global threshold restated for a shard whose page 0 is global page
+    `base` (hx_quest_localize): keys with local indices select exactly the
+    global choice's pages in the shard."""
+    if T in (0, (1 << 64) - 1):
+        return T
+    kT, low = T >> 32, T & 0xFFFFFFFF
+    if kT == 0xFFFFFFFF:
+        return T
+    gmax = (~low) & 0xFFFFFFFF
+    if gmax < base:
+        return (kT + 1) << 32
+    return (kT << 32) | ((~(gmax - base)) & 0xFFFFFFFF)
+
+
+def select_by_threshold(scores_1d, T: int, sink_pages: int):
+    """Ascending local pages: the sinks and every other page with key >= T."""
+    s = np.asarray(scores_1d)
+    n = len(s)
+    sinks = max(0, min(sink_pages, n))
+    keys = keys64(s)
+    chosen = np.nonzero(keys[sinks:] >= np.uint64(T))[0] + sinks
+    return np.concatenate([np.arange(sinks), chosen]).astype(np.int64)
+
+
+def global_selection_per_shard(scores_1d, n_ranks: int, k: int, sink_pages: int):
+    """The single-GPU selection split at the shard bounds, as local indices."""
+    sel = select_pages(scores_1d, k, sink_pages)
+    b = shard_bounds(len(scores_1d), n_ranks)
+    return [sel[(sel >= b[r]) & (sel < b[r + 1])] - b[r] for r in range(n_ranks)]
+
+
+def slice_counts(local_sel, n: int, sinks: int, C: int):
+    """Exclusive prefix (C + 1 entries) of the selected non-sink pages per
+    slice of ceil((n - sinks) / C) pages (the decode's slices)."""
+    n_ns = n - sinks
+    per = (n_ns + C - 1) // C if n_ns > 0 else 1
+    sel = np.asarray(local_sel)
+    sel = sel[sel >= sinks]
+    cnt = np.bincount((sel - sinks) // per, minlength=C)[:C]
+    return np.concatenate([[0], np.cumsum(cnt)]).astype(np.int64)
+
+
+def shard_sinks(sink_pages: int, base: int, n: int) -> int:
+    """The global sinks that fall on a shard of n pages starting at `base`."""
+    return max(0, min(sink_pages - base, n))

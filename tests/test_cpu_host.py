@@ -142,3 +142,54 @@ def test_split_kv_exchange_two_gloo_ranks(tmp_path):
         got = np.load(tmp_path / f"r{r}.npy")
         np.testing.assert_allclose(got[:64].reshape(4, 16), o_ref, atol=1e-5)
         np.testing.assert_allclose(got[64:], lse_ref, atol=1e-5)
+
+
+def test_global_selection_shard_thresholds_match_one_gpu():
+    """The rule hx_quest_localize applies: a single-GPU threshold restated per
+    shard selects, with local page indices, exactly the single-GPU choice's
+    pages on that shard (ties across shard edges, k = 0, k >= n, sinks
+    spilling past the first shard)."""
+    from oracle import quest as oq
+    rng = np.random.default_rng(7)
+    for trial in range(1500):
+        R, n = int(rng.integers(1, 7)), int(rng.integers(1, 48))
+        N = R * n
+        s = (np.round(rng.standard_normal(N) * rng.choice([0.5, 2.0, 8.0])) / 4).astype(np.float32)
+        if trial % 7 == 0:
+            s[:] = 1.0
+        k, sinks = int(rng.integers(0, N + 3)), int(rng.integers(0, 6))
+        T = oq.threshold64(s, k, sinks)
+        np.testing.assert_array_equal(oq.select_by_threshold(s, T, sinks), oq.select_pages(s, k, sinks))
+        want = oq.global_selection_per_shard(s, R, k, sinks)
+        b = oq.shard_bounds(N, R)
+        for r in range(R):
+            ls = oq.shard_sinks(sinks, b[r], b[r + 1] - b[r])
+            got = oq.select_by_threshold(s[b[r]:b[r + 1]], oq.shard_threshold(T, b[r]), ls)
+            np.testing.assert_array_equal(got, want[r])
+
+
+def _gather_worker(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from kvquant.splitkv import gather_score_rows
+        B, H, n = 2, 3, 5
+        loc = torch.arange(B * H * n, dtype=torch.float32).view(B, H, n) + 1000 * rank
+        gathered = torch.empty((world, B * H, n))
+        glob = torch.empty((B, H, world * n))
+        gather_score_rows(loc, gathered, glob)
+        np.save(os.path.join(result_dir, f"g{rank}.npy"), glob.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_global_selection_score_gather_two_gloo_ranks(tmp_path):
+    """The score gather of the global selection puts rank r's pages of every
+    (b, h) row at global pages r*n .. r*n + n - 1, on every rank."""
+    port = _free_port()
+    mp.start_processes(_gather_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    B, H, n = 2, 3, 5
+    base = np.arange(B * H * n, dtype=np.float32).reshape(B, H, n)
+    want = np.concatenate([base, base + 1000], axis=2)
+    for r in range(2):
+        np.testing.assert_array_equal(np.load(tmp_path / f"g{r}.npy"), want)

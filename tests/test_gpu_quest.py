@@ -173,13 +173,14 @@ def test_select_top_blocks_for_layer_planted_block_and_sinks():
     pool.check()
 
 
+@pytest.mark.parametrize("P", [2000, 20000])   # one CTA per row; one CTA per 1024 pages
 @pytest.mark.parametrize("case", ["wide", "anchor_low", "anchor_high", "dup_wide", "negative"])
-def test_threshold_anchored_bins_wide_ranges(case):
+def test_threshold_anchored_bins_wide_ranges(case, P):
     """The histogram bins are centred on the first non-sink page's score and
     clamp beyond 16 octaves; scores far from it (or a boundary inside a
     clamped end bin) must still give the exact top-k."""
     import quest
-    P, H, sinks, k = 20000, 3, 4, 5003
+    H, sinks, k = 3, 4, P // 4 + 3
     rng = np.random.default_rng({"wide": 1, "anchor_low": 2, "anchor_high": 3, "dup_wide": 4, "negative": 5}[case])
     if case == "wide":         # log-uniform over 200 octaves, both signs
         b = np.sign(rng.standard_normal((P, H))) * np.exp2(rng.uniform(-100, 100, (P, H)))
