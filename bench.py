@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="split-KV exchange: peer-memory merge kernel, or NCCL all-gather + merge")
     ap.add_argument("--profile", action="store_true", help="setup + warmup + steps only (for ncu)")
+    ap.add_argument("--decode-cores", choices=["tensor", "cuda"], default="tensor",
+                    help="decode QK / PV on the tensor cores (mma.sync) or as FFMA on the CUDA cores (comparison)")
     ap.add_argument("--select", choices=["shard", "global"], default="shard",
                     help="N > 1: top-K per shard (the default), or the single-GPU top-K over every shard's pages")
     return ap.parse_args()
@@ -287,6 +289,7 @@ def build_world(args, rank, world, device):
         pack_bytes += shard.n_pages * H * 2 * D * 2 * 2                  # stats read + written
         pack_bytes += 4 * int(lay.dir[:, :, :, 2].to(torch.int64).sum())  # outlier entries written
     return dict(pool=pool, shard=shard, qs=qs, bt=bt, sl=sl, k=kk, ns=ns, per_layer=per_layer, gsel=gsel,
+                cores=args.decode_cores,
                 pack=dict(ms=pack_ms, tokens=pack_tokens, bytes=pack_bytes), scales=scales, layout=layout)
 
 
@@ -331,7 +334,7 @@ def make_step(W, world, group, timing=None):
             else:
                 o_dst, lse_dst = o_loc[li], lse_loc[li]
             fused.decode(pool, li, q_all[li], bt, sl, sel, page_begin=shard.page_begin, n_splits=W["ns"],
-                         o=o_dst, lse=lse_dst)
+                         o=o_dst, lse=lse_dst, cores=W.get("cores", "tensor"))
             if timing is not None:
                 timing["ev"][li][2].record()
             if world > 1:
@@ -1018,7 +1021,7 @@ def run_ours(args):
             "data": "synthetic (seeded N(0,1) x log-uniform channel scales, x10 outliers; random queries)",
             "config": workload(args, world),
             "run": {"cuda_graph": use_graph, "n_splits_per_head": W["ns"], "steps_replayed": args.steps,
-                    "exchange": exchange,
+                    "exchange": exchange, "decode_cores": W["cores"],
                     "selection": ("top-K of the whole sequence (one GPU's)" if world == 1 or W.get("gsel") is not None
                                   else "top-K of each shard's pages")},
             "roofline": roofline(dom_b, dom_ms, peak, peak_src, dom, read_traffic(dom)),

@@ -47,6 +47,7 @@ struct DecodeParams {
   const int32_t* seq_lens;
   int page_begin, max_pages, sel_mode;
   int vphys;  // V positions from the physical page (HX_VPOS_PHYSICAL)
+  int cores;  // QK and PV on CUDA cores (HX_DECODE_CUDA_CORES)
   const float* scores;
   const uint64_t* thresh;
   int sinks_req;
@@ -99,6 +100,17 @@ HX_DEVINL uint16_t lds16(uint32_t addr) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
+}
+// four fp16 at a shared address (8-byte aligned) as floats
+HX_DEVINL void lds_h4(uint32_t addr, float (&f)[4]) {
+  uint32_t a, b;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr));
+  const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&a));
+  const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&b));
+  f[0] = lo.x;
+  f[1] = lo.y;
+  f[2] = hi.x;
+  f[3] = hi.y;
 }
 
 // 8 levels for 8 consecutive 4-bit codes of word w (channels c0 .. c0+7):
@@ -213,7 +225,9 @@ HX_DEVINL void patch_tile(uint32_t tile0, const uint32_t* staged, const uint32_t
 HX_DEVINL uint32_t stage_k(uint32_t cntk) { return min((cntk + 3u) & ~3u, (uint32_t)ENTCAP); }
 HX_DEVINL uint32_t stage_v(uint32_t ek, uint32_t cntv) { return min((cntv + 3u) & ~3u, (uint32_t)ENTCAP - ek); }
 
-template <int BK, int BV>
+// FMA: QK and PV in fp32 FFMA on the CUDA cores instead of mma.sync (the
+// same pipeline, dequant, tile and softmax state; the comparison variant).
+template <int BK, int BV, bool FMA>
 __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   CtaSmem& sm = *reinterpret_cast<CtaSmem*>(smem_raw);
@@ -308,10 +322,19 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
     tqk = tile0 + 256u * rk + 16u * ((lane >> 4) ^ (rk & 7));
     tpv = tile0 + 256u * rv + 16u * (((lane >> 3) & 1) ^ (rv & 7));
   }
-  // query fragments (B operand, k = channel, n = head column)
+  // query fragments (B operand, k = channel, n = head column); for FMA the
+  // lane's channels 4 lane .. 4 lane + 3 of every head column, as floats
   const int g = lane >> 2, qd = lane & 3;
   uint32_t bq[8][2];
-  {
+  float qf[8][4];
+  if constexpr (FMA) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int64_t qrow = ((int64_t)b * H * G + (int64_t)h * G + c) * DD + 4 * lane;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qf[c][i] = c < G ? __half2float(__ushort_as_half(p.q[qrow + i])) : 0.0f;
+    }
+  } else {
     const int64_t qrow = ((int64_t)b * H * G + (int64_t)h * G + g) * DD;
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
@@ -561,18 +584,74 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       patch_tile(tile0, ws.ent[st], p.pool.arena + offk, cntk, ek, lane, p.err);
       __syncwarp();
 
-      // ---- S^T = K . Q^T  (16 tokens x 8 head columns), two accumulator chains
-      float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // ---- S^T = K . Q^T  (16 tokens x 8 head columns)
+      float x0, x1, x2, x3;  // S[g][2qd], S[g][2qd + 1], S[g + 8][2qd], S[g + 8][2qd + 1]
+      if constexpr (FMA) {
+        // the lane's 4 channels of 2 tokens at a time against its q columns;
+        // a halving butterfly sums each (token, column) over the warp and
+        // leaves lanes l and l ^ 1 with S[2 grp + (l >> 4)][(l >> 1) & 7]
+        float r[8];
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        uint32_t a[4];
-        ldsm_x4(a, tqk ^ (16u * ((2 * ks) ^ (4 * (ks >> 2)))));
-        if (ks & 1) mma_16816(sb, a, bq[ks][0], bq[ks][1]);
-        else mma_16816(sa, a, bq[ks][0], bq[ks][1]);
+        for (int grp = 0; grp < 8; ++grp) {
+          float a[16];
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt) {
+            const int tk = 2 * grp + tt;
+            const uint32_t c = (uint32_t)lane >> 1;
+            float kf[4];
+            lds_h4(tile0 + 256u * tk + 16u * (c ^ (uint32_t)(tk & 7) ^ (4u * (c >> 3))) + 8u * (lane & 1), kf);
+#pragma unroll
+            for (int col = 0; col < 8; ++col)
+              a[8 * tt + col] =
+                  fmaf(kf[3], qf[col][3], fmaf(kf[2], qf[col][2], fmaf(kf[1], qf[col][1], kf[0] * qf[col][0])));
+          }
+#pragma unroll
+          for (int m = 8; m >= 1; m >>= 1) {  // lane bits 4, 3, 2, 1 take index bits 3, 2, 1, 0
+            const bool upper = (lane & (2 * m)) != 0;
+#pragma unroll
+            for (int i = 0; i < m; ++i) {
+              const float send = upper ? a[i] : a[i + m];
+              const float keep = upper ? a[i + m] : a[i];
+              a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2 * m);
+            }
+          }
+          r[grp] = a[0] + __shfl_xor_sync(0xffffffffu, a[0], 1);
+        }
+        // token g is in group g >> 1 (g + 8 in group 4 + (g >> 1)), at lane
+        // (g & 1) << 4 | column << 1
+        const int src = ((g & 1) << 4) | (qd << 2);
+        const int gi = g >> 1;
+        float y[4], z[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          y[u] = __shfl_sync(0xffffffffu, r[u], src);
+          z[u] = __shfl_sync(0xffffffffu, r[u], src | 2);
+        }
+        x0 = (gi == 0 ? y[0] : gi == 1 ? y[1] : gi == 2 ? y[2] : y[3]) * p.scale_log2;
+        x1 = (gi == 0 ? z[0] : gi == 1 ? z[1] : gi == 2 ? z[2] : z[3]) * p.scale_log2;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          y[u] = __shfl_sync(0xffffffffu, r[4 + u], src);
+          z[u] = __shfl_sync(0xffffffffu, r[4 + u], src | 2);
+        }
+        x2 = (gi == 0 ? y[0] : gi == 1 ? y[1] : gi == 2 ? y[2] : y[3]) * p.scale_log2;
+        x3 = (gi == 0 ? z[0] : gi == 1 ? z[1] : gi == 2 ? z[2] : z[3]) * p.scale_log2;
+      } else {
+        // two accumulator chains
+        float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          uint32_t a[4];
+          ldsm_x4(a, tqk ^ (16u * ((2 * ks) ^ (4 * (ks >> 2)))));
+          if (ks & 1) mma_16816(sb, a, bq[ks][0], bq[ks][1]);
+          else mma_16816(sa, a, bq[ks][0], bq[ks][1]);
+        }
+        x0 = (sa[0] + sb[0]) * p.scale_log2;
+        x1 = (sa[1] + sb[1]) * p.scale_log2;
+        x2 = (sa[2] + sb[2]) * p.scale_log2;
+        x3 = (sa[3] + sb[3]) * p.scale_log2;
       }
       // ---- online softmax (exp2 domain); rows = tokens g, g+8; cols = 2qd, 2qd+1
-      float x0 = (sa[0] + sb[0]) * p.scale_log2, x1 = (sa[1] + sb[1]) * p.scale_log2;
-      float x2 = (sa[2] + sb[2]) * p.scale_log2, x3 = (sa[3] + sb[3]) * p.scale_log2;
       if (g >= valid) x0 = x1 = -INFINITY;
       if (g + 8 >= valid) x2 = x3 = -INFINITY;
       // the running max moves only when a score passes it by more than 2^8
@@ -604,14 +683,19 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       l0 += p0 + p2;
       l1 += p1 + p3;
       // P^T as the B operand (k = token, n = head column): hi and lo halves
-      const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
-      const __half h2 = __float2half_rn(p2), h3 = __float2half_rn(p3);
-      const uint32_t phi_top = pack_u16x2(__half_as_ushort(h0), __half_as_ushort(h1));
-      const uint32_t phi_bot = pack_u16x2(__half_as_ushort(h2), __half_as_ushort(h3));
-      const uint32_t plo_top = pack_half2(p0 - __half2float(h0), p1 - __half2float(h1));
-      const uint32_t plo_bot = pack_half2(p2 - __half2float(h2), p3 - __half2float(h3));
-      const uint32_t bh0 = movmatrix_trans(phi_top), bh1 = movmatrix_trans(phi_bot);
-      const uint32_t bl0 = movmatrix_trans(plo_top), bl1 = movmatrix_trans(plo_bot);
+      uint32_t bh0 = 0u, bh1 = 0u, bl0 = 0u, bl1 = 0u;
+      if constexpr (!FMA) {
+        const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
+        const __half h2 = __float2half_rn(p2), h3 = __float2half_rn(p3);
+        const uint32_t phi_top = pack_u16x2(__half_as_ushort(h0), __half_as_ushort(h1));
+        const uint32_t phi_bot = pack_u16x2(__half_as_ushort(h2), __half_as_ushort(h3));
+        const uint32_t plo_top = pack_half2(p0 - __half2float(h0), p1 - __half2float(h1));
+        const uint32_t plo_bot = pack_half2(p2 - __half2float(h2), p3 - __half2float(h3));
+        bh0 = movmatrix_trans(phi_top);
+        bh1 = movmatrix_trans(phi_bot);
+        bl0 = movmatrix_trans(plo_top);
+        bl1 = movmatrix_trans(plo_bot);
+      }
 
       // ---- V tile: per-token LUT (row min(pos, t_cal - 1))
       const bool vshared = pos0 >= Tc;
@@ -677,12 +761,36 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
       __syncwarp();
 
       // ---- O^T += V^T . P^T  (128 channels x 8 head columns)
+      if constexpr (FMA) {
+        // lane (g, qd) keeps head columns 2qd, 2qd + 1 of channels 32k + 4g + i
+        // (k, i < 4) in oacc[q >> 1][2 (q & 1) + column], q = 4k + i; token
+        // tk's P comes from lane 4 (tk & 7) + qd (p0, p1 below token 8, else p2, p3)
+#pragma unroll 1
+        for (int tk = 0; tk < DS; ++tk) {
+          const int srcl = 4 * (tk & 7) + qd;
+          const float pc0 = __shfl_sync(0xffffffffu, tk < 8 ? p0 : p2, srcl);
+          const float pc1 = __shfl_sync(0xffffffffu, tk < 8 ? p1 : p3, srcl);
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        uint32_t a[4];
-        ldsm_x4_trans(a, tpv ^ (16u * ((2 * mt) ^ (4 * (mt >> 2)))));
-        mma_16816(oacc[mt], a, bh0, bh1);
-        mma_16816(oacc[mt], a, bl0, bl1);
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t c = 4u * k + ((uint32_t)g >> 1);
+            float vf[4];
+            lds_h4(tile0 + 256u * tk + 16u * (c ^ (uint32_t)(tk & 7) ^ (4u * (c >> 3))) + 8u * (g & 1), vf);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int q = 4 * k + i;
+              oacc[q >> 1][2 * (q & 1)] = fmaf(pc0, vf[i], oacc[q >> 1][2 * (q & 1)]);
+              oacc[q >> 1][2 * (q & 1) + 1] = fmaf(pc1, vf[i], oacc[q >> 1][2 * (q & 1) + 1]);
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          uint32_t a[4];
+          ldsm_x4_trans(a, tpv ^ (16u * ((2 * mt) ^ (4 * (mt >> 2)))));
+          mma_16816(oacc[mt], a, bh0, bh1);
+          mma_16816(oacc[mt], a, bl0, bl1);
+        }
       }
       __syncwarp();
     }
@@ -707,13 +815,22 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
   float* wO = reinterpret_cast<float*>(ws.raw);     // [8][128] floats = 4 KB
   float* wml = reinterpret_cast<float*>(ws.vlut);   // m[8], l[8]
+  if constexpr (FMA) {
 #pragma unroll
-  for (int mt = 0; mt < 8; ++mt) {
-    const int d = 16 * mt + g;
-    wO[(2 * qd) * DD + d] = oacc[mt][0];
-    wO[(2 * qd + 1) * DD + d] = oacc[mt][1];
-    wO[(2 * qd) * DD + d + 8] = oacc[mt][2];
-    wO[(2 * qd + 1) * DD + d + 8] = oacc[mt][3];
+    for (int q = 0; q < 16; ++q) {
+      const int d = 32 * (q >> 2) + 4 * g + (q & 3);
+      wO[(2 * qd) * DD + d] = oacc[q >> 1][2 * (q & 1)];
+      wO[(2 * qd + 1) * DD + d] = oacc[q >> 1][2 * (q & 1) + 1];
+    }
+  } else {
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int d = 16 * mt + g;
+      wO[(2 * qd) * DD + d] = oacc[mt][0];
+      wO[(2 * qd + 1) * DD + d] = oacc[mt][1];
+      wO[(2 * qd) * DD + d + 8] = oacc[mt][2];
+      wO[(2 * qd + 1) * DD + d + 8] = oacc[mt][3];
+    }
   }
   if (g == 0) {
     wml[2 * qd] = m0;
@@ -949,7 +1066,7 @@ using namespace hx;
 
 static inline cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-template <int BK, int BV>
+template <int BK, int BV, bool FMA>
 static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
   const size_t smem = sizeof(CtaSmem);
   // per device, once: the attribute call is idempotent, so two threads that
@@ -958,13 +1075,13 @@ static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_ERR_LAUNCH;
   if (!attr_set[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(decode_kernel<BK, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(decode_kernel<BK, BV, FMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
       return HX_ERR_LAUNCH;
     attr_set[dev].store(true, std::memory_order_release);
   }
   dim3 grid(p.n_splits, H, p.B);
-  if (hx_launch_pdl(decode_kernel<BK, BV>, grid, dim3(NT), smem, s, p) != cudaSuccess) {
+  if (hx_launch_pdl(decode_kernel<BK, BV, FMA>, grid, dim3(NT), smem, s, p) != cudaSuccess) {
     (void)cudaGetLastError();
     return HX_ERR_LAUNCH;
   }
@@ -1005,8 +1122,9 @@ static int prepare_decode(DecodeParams& p, const hx_pool_layer* pool, const hx_l
   if (sc->levels_k < 1 || sc->levels_v < 1 || sc->levels_k > (1 << pool->bits_k) ||
       sc->levels_v > (1 << pool->bits_v) || sc->t_cal < 1)
     return HX_ERR_ARG;
-  if ((sel_mode & ~(HX_SEL_MODE_MASK | HX_VPOS_PHYSICAL)) != 0) return HX_ERR_ARG;
+  if ((sel_mode & ~(HX_SEL_MODE_MASK | HX_VPOS_PHYSICAL | HX_DECODE_CUDA_CORES)) != 0) return HX_ERR_ARG;
   const int vphys = (sel_mode & HX_VPOS_PHYSICAL) ? 1 : 0;
+  const int cores = (sel_mode & HX_DECODE_CUDA_CORES) ? 1 : 0;
   sel_mode &= HX_SEL_MODE_MASK;
   if (sel_mode < 0 || sel_mode > 3) return HX_ERR_ARG;
   if (sel_mode == HX_SEL_THRESHOLD && (!scores || !thresh)) return HX_ERR_ARG;
@@ -1028,6 +1146,7 @@ static int prepare_decode(DecodeParams& p, const hx_pool_layer* pool, const hx_l
   p.max_pages = max_pages;
   p.sel_mode = sel_mode;
   p.vphys = vphys;
+  p.cores = cores;
   p.scores = scores;
   p.thresh = thresh;
   p.sinks_req = sink_pages;
@@ -1048,10 +1167,16 @@ static int launch_prepared(DecodeParams& p, void* scratch, cudaStream_t s) {
   p.ctr = reinterpret_cast<uint32_t*>(scratch);
   p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCtrBytes);
   const int H = p.pool.num_kv_heads;
-  if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4>(p, H, s);
-  if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2>(p, H, s);
-  if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4>(p, H, s);
-  return launch_decode<2, 2>(p, H, s);
+  if (p.cores) {
+    if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4, true>(p, H, s);
+    if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2, true>(p, H, s);
+    if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4, true>(p, H, s);
+    return launch_decode<2, 2, true>(p, H, s);
+  }
+  if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4, false>(p, H, s);
+  if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2, false>(p, H, s);
+  if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4, false>(p, H, s);
+  return launch_decode<2, 2, false>(p, H, s);
 }
 
 HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc, const uint16_t* q,

@@ -22,6 +22,7 @@ DEV_ERR = {0x1: "outlier arena full", 0x2: "index out of range", 0x4: "bounded w
            0x8: "selection threshold not isolated"}
 SEL_DENSE, SEL_THRESHOLD, SEL_LIST, SEL_SLICES = 0, 1, 2, 3
 VPOS_PHYSICAL = 0x100  # OR-ed into the decode's sel_mode (helix_kv.h)
+DECODE_CUDA_CORES = 0x200  # OR-ed into sel_mode: QK and PV in FFMA (helix_kv.h)
 
 c_vp, c_i32, c_i64, c_f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
 

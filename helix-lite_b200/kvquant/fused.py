@@ -161,7 +161,8 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
            seq_lens: torch.Tensor, selection: Selection | None = None, *, lists: torch.Tensor | None = None,
            list_counts: torch.Tensor | None = None, page_begin: int = 0, max_pages: int | None = None,
            n_splits: int | None = None, softmax_scale: float | None = None, out16: torch.Tensor | None = None,
-           o: torch.Tensor | None = None, lse: torch.Tensor | None = None, v_pos: str = "logical"):
+           o: torch.Tensor | None = None, lse: torch.Tensor | None = None, v_pos: str = "logical",
+           cores: str = "tensor"):
     """Fused-dequant decode attention; returns (o (B, Hq, D) fp32, lse (B, Hq)).
 
     Pages attended: every page (no selection), the Quest selection (split
@@ -169,8 +170,12 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
     lists when it has them, else over the sequence), or explicit per-(b, h)
     logical page lists (``lists`` (B, H, L) int32 with ``list_counts`` (B,
     H)). ``page_begin`` is the absolute logical page of this pool's page 0
-    (split-KV shards), used for V's position clamp.
+    (split-KV shards), used for V's position clamp. ``cores="cuda"`` runs QK
+    and PV as fp32 FFMA on the CUDA cores (the comparison variant) instead of
+    mma.sync on the tensor cores.
     """
+    if cores not in ("tensor", "cuda"):
+        raise ValueError("cores must be 'tensor' or 'cuda'")
     dev = pool.device
     q = query.to(device=dev, dtype=torch.float16).contiguous()
     B, Hq, D = q.shape
@@ -216,7 +221,8 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
     with torch.cuda.device(dev):
         call("hx_decode_attn", stream(dev), ctypes_ref(pool.layers[layer_idx].struct), ctypes_ref(st_scales),
              ptr(q), B, Hq // H, scale, ptr(bt), bt.shape[1], ptr(sl), int(page_begin), mp,
-             mode | (hxlib.VPOS_PHYSICAL if v_pos == "physical" else 0),
+             mode | (hxlib.VPOS_PHYSICAL if v_pos == "physical" else 0)
+             | (hxlib.DECODE_CUDA_CORES if cores == "cuda" else 0),
              ptr(selection.scores) if selection is not None else None,
              ptr(selection.thresh) if selection is not None else None,
              selection.sink_pages if selection is not None else 0,

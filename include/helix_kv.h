@@ -296,6 +296,10 @@ HX_API int hx_quest_localize(void* stream, const uint64_t* thresh_global, const 
  * (compact_backend.py:157-167, compact_pool.py:370-372, quest_selector.py:89).
  * Without it the row is that of the logical position (page_begin + j) * 16 + t. */
 #define HX_VPOS_PHYSICAL 0x100
+/* OR-ed into sel_mode: QK and PV in fp32 FFMA on the CUDA cores instead of
+ * the tensor cores (mma.sync), with the same pipeline, dequant and softmax.
+ * Slower; kept as the comparison the design choice rests on. */
+#define HX_DECODE_CUDA_CORES 0x200
 
 /* Scratch bytes hx_decode_attn needs for B sequences, H heads, n_splits. */
 HX_API int64_t hx_decode_scratch_bytes(int32_t B, int32_t H, int32_t n_splits);

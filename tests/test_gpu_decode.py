@@ -19,10 +19,16 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-3  # max-abs on the normalised attention output
 
 
-def _build(layout, n_tokens, seed, B=1, t_cal=4096, pages_extra=0, shuffle=False):
+def _build(layout, n_tokens, seed, B=1, t_cal=4096, pages_extra=0, shuffle=False, v_layout=None):
+    """A pool over `layout`; with `v_layout` the V scales (and V code width)
+    of each layer come from that layout instead."""
     from kvquant.synthetic import make_kv, make_scales
     H, D, S = 4, 128, 16
     sc = make_scales(layout, H, D, t_cal=t_cal, seed=seed)
+    if v_layout is not None:
+        sv = make_scales(v_layout, H, D, t_cal=t_cal, seed=seed + 7)
+        for li in range(len(layout)):
+            sc.per_layer_values[li] = sv.per_layer_values[li]
     n_pages = [-(-n // S) for n in n_tokens]
     NB = sum(n_pages) + pages_extra
     gpu, orc = make_pools(sc, NB, S, H, D)
@@ -77,6 +83,31 @@ def test_dense_decode_matches_oracle(layout_name):
     ro, rl = _oracle_out(orc, 0, q, bt, sl)
     assert np.abs(np16(o) - ro).max() < TOL
     np.testing.assert_allclose(np16(lse), rl, atol=1e-3)
+
+
+@pytest.mark.parametrize("bits", [(4, 4), (4, 2), (2, 4), (2, 2)])
+def test_cuda_core_decode_matches_oracle(bits):
+    """The CUDA-core (FFMA) variant of the decode, dense and over a Quest
+    selection, against the same oracle; K and V at every pair of widths."""
+    from kvquant import fused
+    from kvquant.synthetic import NUQ2, NUQ4
+    lay = {4: NUQ4, 2: NUQ2}
+    gpu, orc, bt, sl = _build([lay[bits[0]]], [6000 - 3], seed=25, v_layout=[lay[bits[1]]])
+    assert (gpu.layers[0].bits_k, gpu.layers[0].bits_v) == bits
+    q = _query(1, 7, 26)
+    o, lse = fused.decode(gpu, 0, q, bt, sl, cores="cuda")
+    ro, rl = _oracle_out(orc, 0, q, bt, sl)
+    assert np.abs(np16(o) - ro).max() < TOL
+    np.testing.assert_allclose(np16(lse), rl, atol=1e-3)
+    sel = fused.quest_select(gpu, 0, q, bt, sl, top_frac=(1, 4), sink_pages=4)
+    lists, counts = fused.selected_lists(sel)
+    o2, _ = fused.decode(gpu, 0, q, bt, sl, sel, cores="cuda")
+    o3, _ = fused.decode(gpu, 0, q, bt, sl, sel)
+    gpu.check()
+    pages = [[np16(lists[0, h, :int(counts[0, h])]) for h in range(4)]]
+    ro2, _ = _oracle_out(orc, 0, q, bt, sl, pages)
+    assert np.abs(np16(o2) - ro2).max() < TOL
+    assert np.abs(np16(o2) - np16(o3)).max() < TOL
 
 
 def test_quest_decode_matches_oracle_config3_shape():
