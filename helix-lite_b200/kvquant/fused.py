@@ -231,6 +231,46 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
     return o, lse
 
 
+def prefill(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, query_start: torch.Tensor,
+            block_table: torch.Tensor, seq_lens: torch.Tensor, *, max_query_len: int | None = None,
+            softmax_scale: float | None = None, v_pos: str = "logical", out: torch.Tensor | None = None,
+            lse: torch.Tensor | None = None, out32: torch.Tensor | None = None):
+    """Chunked-prefill attention read from the compact pool (one kernel).
+
+    query (Tq, Hq, D) fp16: sequence b's chunk is rows query_start[b] ..
+    query_start[b + 1] - 1, the last tokens of its seq_lens[b], already
+    written to the pool (write_kv); each query attends causally to every
+    earlier token of its sequence and to itself. Returns (out (Tq, Hq, D)
+    fp16, lse (Tq, Hq) fp32 natural log); ``out32`` (Tq, Hq, D) fp32, when
+    given, receives the output before its fp16 rounding. The reference's prefill reads
+    vLLM's fp16 cache instead (src/kvquant/compact_backend.py:12-15).
+    """
+    dev = pool.device
+    q = query.to(device=dev, dtype=torch.float16).contiguous()
+    Tq, Hq, D = q.shape
+    H = pool.num_kv_heads
+    if Hq % H:
+        raise ValueError("query heads must be a multiple of KV heads")
+    qs = _i32(query_start, dev)
+    bt = _i32(block_table, dev)
+    sl = _i32(seq_lens, dev)
+    B = qs.shape[0] - 1
+    if max_query_len is None:
+        max_query_len = int((qs[1:] - qs[:-1]).max().item()) if B > 0 else 0
+    scale = float(softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D))
+    if out is None:
+        out = torch.empty((Tq, Hq, D), dtype=torch.float16, device=dev)
+    if lse is None:
+        lse = torch.empty((Tq, Hq), dtype=torch.float32, device=dev)
+    st_scales, _keep = pool.scales.device_layer(layer_idx, dev)
+    with torch.cuda.device(dev):
+        call("hx_prefill_attn", stream(dev), ctypes_ref(pool.layers[layer_idx].struct), ctypes_ref(st_scales),
+             ptr(q), ptr(qs), B, Hq // H, scale, ptr(bt), bt.shape[1], ptr(sl), int(max_query_len),
+             hxlib.VPOS_PHYSICAL if v_pos == "physical" else 0, ptr(out), ptr(out32), ptr(lse),
+             ptr(hxlib.err_word(dev)))
+    return out, lse
+
+
 def merge_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, out16: torch.Tensor | None = None):
     """Merge R shards' normalised (o, lse): (R, N, D), (R, N) -> (N, D), (N,)."""
     R, N, D = o_parts.shape

@@ -335,6 +335,28 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
                           uint32_t* dev_err);
 
 /*
+ * Chunked-prefill attention over the compact pool. q (Tq, H*group, D) fp16
+ * holds B sequences' query tokens back to back: sequence b's are rows
+ * q_start[b] .. q_start[b+1] - 1 (q_start (B+1) int32, device), the last
+ * q_len_b tokens of its seq_lens[b] tokens, already packed into the pool
+ * (hx_pack_append). Query token i of sequence b (position seq_lens[b] -
+ * q_len_b + i) attends causally to positions 0 .. its own, read and
+ * dequantised from the pages block_table[b*bt_stride + j]; V rows by the
+ * logical position, or the physical one with HX_VPOS_PHYSICAL in flags.
+ * max_q_len bounds q_len_b (grid size). Writes out16 (Tq, H*group, D) fp16
+ * and, when non-NULL, out32 (the same in fp32) and lse (Tq, H*group) fp32
+ * natural log. D = 128, page
+ * size 16. No reference counterpart: the reference's prefill reads vLLM's
+ * fp16 cache, which it keeps beside the compact pool for that reason
+ * (src/kvquant/compact_backend.py:12-15).
+ */
+HX_API int hx_prefill_attn(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
+                           const uint16_t* q, const int32_t* q_start, int32_t B, int32_t group,
+                           float softmax_scale, const int32_t* block_table, int32_t bt_stride,
+                           const int32_t* seq_lens, int32_t max_q_len, int32_t flags,
+                           uint16_t* out16, float* out32, float* lse, uint32_t* dev_err);
+
+/*
  * hx_decode_attn without a caller scratch buffer: no counterpart in the
  * reference. Its scratch is a fixed array inside this library (64 KB of split
  * counters + 1024 split partials, about 4.3 MB per GPU that loads the
