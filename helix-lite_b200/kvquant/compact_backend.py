@@ -20,6 +20,18 @@ K/V. Prefill, profiling runs and attention features the fused kernel does
 not implement (sliding window, ALiBi, logits soft cap, attention sinks,
 cross attention) go to FlashAttention unchanged.
 
+With ``fp16_cache=False`` vLLM keeps no fp16 cache at all (the reference's
+planned custom backend, src/kvquant/PHASE_1B_DESIGN.md:81-88): each decoder
+layer's KV-cache spec asks for one KV head of one channel, so vLLM budgets
+64 bytes per block and layer instead of the fp16 page, the backend's
+``get_kv_cache_shape`` returns the matching (2, blocks, block_size, 1, 1)
+placeholder, and the impl never touches ``kv_cache``: the cache update
+packs into the compact pool only, decode steps run as above, and prefill or
+mixed batches run the chunked-prefill kernel over the pool (every query
+token attends causally to its sequence's packed tokens). vLLM must then be
+given at most the pool's block count (``num_gpu_blocks_override``); the
+kernels flag any block id past it.
+
 The base classes are vLLM's (``vllm.v1.attention.backends.flash_attn``);
 ``backend_cls`` / ``impl_cls`` may be passed to install against other
 classes with the same interface (the tests do).
@@ -43,6 +55,7 @@ _SINK_BLOCKS: int = 4
 _GQA: str = "mean"         # how the group's queries bound a page (the reference hook: mean)
 _LAYER_INDEX: dict[str, int] = {}
 _IMPL_CLS = None
+_FP16_CACHE: bool = True   # False: vLLM keeps no fp16 cache; prefill reads the pool
 
 
 def layer_index(layer) -> int | None:
@@ -77,7 +90,8 @@ def make_impl_cls(base):
         can_return_lse_for_decode: bool = True
 
         def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping):
-            super().do_kv_cache_update(layer, key, value, kv_cache, slot_mapping)
+            if _FP16_CACHE:
+                super().do_kv_cache_update(layer, key, value, kv_cache, slot_mapping)
             pool = _POOL
             idx = layer_index(layer)
             n = int(slot_mapping.shape[0])
@@ -101,7 +115,19 @@ def make_impl_cls(base):
                            or getattr(attn_metadata, "seq_lens", None) is None
                            or getattr(attn_metadata, "causal", True) is False
                            or _unsupported(self))
-            if passthrough:
+            if passthrough and not _FP16_CACHE:
+                # no fp16 cache to fall back on: prefill and mixed batches read
+                # the pool; what the kernels do not implement is an error
+                if attn_metadata is None:
+                    return output                 # profiling run: nothing cached yet
+                if (pool is None or idx is None or idx >= pool.num_layers or _unsupported(self)
+                        or output_scale is not None or output_block_scale is not None
+                        or getattr(attn_metadata, "causal", True) is False):
+                    raise NotImplementedError("the compact-pool backend without an fp16 cache supports causal "
+                                              "decoder attention of the pool's layers only")
+                if getattr(attn_metadata, "max_query_len", 0) != 1:
+                    return prefill_into(pool, idx, query, attn_metadata, output, scale=float(self.scale))
+            elif passthrough:
                 return super().forward(layer, query, key, value, kv_cache, attn_metadata, output,
                                        output_scale, output_block_scale)
             return decode_into(pool, idx, query, attn_metadata, output, scale=float(self.scale))
@@ -134,20 +160,63 @@ def decode_into(pool: CompactKVPool, idx: int, query: torch.Tensor, attn_metadat
     return output
 
 
+def prefill_into(pool: CompactKVPool, idx: int, query: torch.Tensor, attn_metadata, output: torch.Tensor,
+                 scale: float) -> torch.Tensor:
+    """Every query token of the batch (prefill chunks and decode tokens alike)
+    attends causally to its sequence's tokens in the pool; written into
+    ``output[:num_actual_tokens]``."""
+    n = int(getattr(attn_metadata, "num_actual_tokens", query.shape[0]))
+    qsl = attn_metadata.query_start_loc
+    B = int(qsl.shape[0]) - 1
+    Hq, D = query.shape[-2], query.shape[-1]
+    out = output[:n].view(n, Hq, D)
+    o16, _ = fused.prefill(pool, idx, query[:n].reshape(n, Hq, D), qsl, attn_metadata.block_table[:B],
+                           attn_metadata.seq_lens[:B], max_query_len=int(attn_metadata.max_query_len),
+                           softmax_scale=scale, v_pos="physical",
+                           out=out if out.dtype == torch.float16 and out.is_contiguous() else None)
+    if o16.data_ptr() != out.data_ptr():
+        out.copy_(o16.to(out.dtype))
+    return output
+
+
+def tiny_kv_cache_spec(spec):
+    """A decoder layer's vLLM KV-cache spec reduced to one KV head of one
+    channel: vLLM then budgets 2 * block_size * dtype bytes per block and
+    layer, and keeps no fp16 K/V (the compact pool holds them)."""
+    import dataclasses
+    kw = {"num_kv_heads": 1, "head_size": 1}
+    if hasattr(spec, "head_size_v"):
+        kw["head_size_v"] = 1
+    return dataclasses.replace(spec, **kw)
+
+
+def tiny_kv_cache_shape(num_blocks: int, block_size: int, num_kv_heads: int = 1, head_size: int = 1,
+                        cache_dtype_str: str = "auto") -> tuple[int, ...]:
+    """FlashAttentionBackend.get_kv_cache_shape's layout at one head of one
+    channel: the placeholder vLLM allocates in place of the fp16 cache."""
+    return (2, num_blocks, block_size, 1, 1)
+
+
 def install_compact_backend(scales_path: str, *, num_layers: int = 28, num_blocks: int = 16_384,
                             block_size: int = 16, num_kv_heads: int = 4, head_size: int = 128,
                             device: str = "cuda:0", top_k_blocks_decode: int = 0, sink_blocks: int = 4,
                             gqa: str = "mean", scales: KVScales | None = None, backend_cls=None,
-                            impl_cls=None) -> None:
+                            impl_cls=None, fp16_cache: bool = True, attention_cls=None) -> None:
     """Allocate the compact pool and route vLLM's FlashAttention backend to
     ``KVQuantCompactImpl`` (compact_backend.py:70-119). Call before building
     the vLLM engine. ``top_k_blocks_decode`` = 0 attends to every block;
-    ``scales`` (already loaded) takes the place of ``scales_path``."""
-    global _POOL, _SCALES, _TOP_K, _SINK_BLOCKS, _GQA, _IMPL_CLS
+    ``scales`` (already loaded) takes the place of ``scales_path``.
+    ``fp16_cache=False`` also removes vLLM's fp16 cache: ``attention_cls``
+    (vLLM's Attention layer by default) reports the tiny KV-cache spec and
+    ``backend_cls`` the tiny shape; prefill then reads the compact pool."""
+    global _POOL, _SCALES, _TOP_K, _SINK_BLOCKS, _GQA, _IMPL_CLS, _FP16_CACHE
     if backend_cls is None or impl_cls is None:
         from vllm.v1.attention.backends.flash_attn import FlashAttentionBackend, FlashAttentionImpl
         backend_cls = backend_cls or FlashAttentionBackend
         impl_cls = impl_cls or FlashAttentionImpl
+    if not fp16_cache and attention_cls is None:
+        from vllm.model_executor.layers.attention.attention import Attention
+        attention_cls = Attention
     sc = scales if scales is not None else KVScales.load(scales_path, map_location=device)
     sc = sc.to(device)
     if sc.num_layers != num_layers:
@@ -161,7 +230,18 @@ def install_compact_backend(scales_path: str, *, num_layers: int = 28, num_block
     _GQA = gqa
     _LAYER_INDEX.clear()
     _IMPL_CLS = make_impl_cls(impl_cls)
+    _FP16_CACHE = bool(fp16_cache)
     backend_cls.get_impl_cls = staticmethod(lambda: _IMPL_CLS)
+    if not fp16_cache:
+        backend_cls.get_kv_cache_shape = staticmethod(tiny_kv_cache_shape)
+        base_spec = getattr(attention_cls, "_hx_base_kv_cache_spec", attention_cls.get_kv_cache_spec)
+
+        def get_kv_cache_spec(self, vllm_config):
+            spec = base_spec(self, vllm_config)
+            return tiny_kv_cache_spec(spec) if spec is not None else None
+
+        attention_cls._hx_base_kv_cache_spec = base_spec
+        attention_cls.get_kv_cache_spec = get_kv_cache_spec
 
 
 def pool() -> CompactKVPool | None:

@@ -180,3 +180,76 @@ def test_hooks_subclass_the_installed_vllm_impl():
     assert list(base)[:8] == ["self", "layer", "query", "key", "value", "kv_cache", "attn_metadata", "output"]
     assert list(inspect.signature(fa.FlashAttentionImpl.do_kv_cache_update).parameters) == \
         ["self", "layer", "key", "value", "kv_cache", "slot_mapping"]
+
+
+class FakeAttention:
+    """Stands in for vLLM's Attention layer: reports an fp16 cache spec."""
+    def get_kv_cache_spec(self, vllm_config):
+        fa = pytest.importorskip("vllm.v1.kv_cache_interface")
+        return fa.FullAttentionSpec(block_size=16, num_kv_heads=4, head_size=128, dtype=torch.float16)
+
+
+def test_no_fp16_cache_install_shrinks_vllm_cache(monkeypatch):
+    """fp16_cache=False: the layer spec asks for one head of one channel (64
+    bytes per block and layer instead of 32 KB) and the backend's shape is the
+    matching placeholder; the impl never calls FlashAttention's cache update."""
+    from kvquant import compact_backend as cb
+    from kvquant.scales import KVScales, PerChannelScale, PerTokenScale
+    H, D, L, Tc = 4, 128, 16, 64
+    ks = PerChannelScale(torch.zeros(H, D, L, dtype=torch.float16), torch.ones(H, D, dtype=torch.float16),
+                         -torch.ones(H, D, dtype=torch.float16), 4)
+    vs = PerTokenScale(torch.zeros(H, Tc, L, dtype=torch.float16), torch.ones(H, Tc, dtype=torch.float16),
+                       -torch.ones(H, Tc, dtype=torch.float16), 4)
+    monkeypatch.setattr(cb, "CompactKVPool", lambda *a, **k: FakePool())
+    backend = type("Backend", (FakeBackend,), {})
+    attn = type("Attn", (FakeAttention,), {})
+    full = FakeAttention().get_kv_cache_spec(None)
+    cb.install_compact_backend("", num_layers=2, device="cpu", scales=KVScales([ks, ks], [vs, vs]),
+                               backend_cls=backend, impl_cls=FakeImpl, fp16_cache=False, attention_cls=attn)
+    try:
+        spec = attn().get_kv_cache_spec(None)
+        assert full.page_size_bytes == 2 * 16 * 4 * 128 * 2
+        assert spec.page_size_bytes == 2 * 16 * 1 * 1 * 2 and spec.block_size == 16
+        assert backend.get_kv_cache_shape(100, 16, 1, 1) == (2, 100, 16, 1, 1)
+        # installing again keeps one level of wrapping
+        cb.install_compact_backend("", num_layers=2, device="cpu", scales=KVScales([ks, ks], [vs, vs]),
+                                   backend_cls=backend, impl_cls=FakeImpl, fp16_cache=False, attention_cls=attn)
+        assert attn().get_kv_cache_spec(None).page_size_bytes == 64
+        impl = backend.get_impl_cls()()
+        key = torch.randn(3, 4, 128)
+        impl.do_kv_cache_update(_layer(1), key, key, None, torch.tensor([5, 6, 7]))
+        assert not impl.calls and cb.pool().writes[0][0] == 1 and cb.pool().writes[0][3] == [5, 6, 7]
+    finally:
+        monkeypatch.setattr(cb, "_FP16_CACHE", True)
+
+
+def test_no_fp16_cache_prefill_reads_the_pool(compact, monkeypatch):
+    """Prefill and mixed batches go to the chunked-prefill kernel with vLLM's
+    query_start_loc / seq_lens / block_table; a profiling run is a no-op and
+    options the kernels lack raise instead of falling back."""
+    cb, pool, calls = compact
+    monkeypatch.setattr(cb, "_FP16_CACHE", False)
+    seen = []
+
+    def prefill(pool_, li, q, qs, bt, sl, **kw):
+        seen.append((li, tuple(q.shape), qs.tolist(), tuple(bt.shape), sl.tolist(), kw["max_query_len"],
+                     kw["v_pos"], kw["softmax_scale"]))
+        return torch.full(q.shape, 0.25, dtype=torch.float16), None
+
+    monkeypatch.setattr(cb.fused, "prefill", prefill, raising=False)
+    impl = cb.make_impl_cls(FakeImpl)()
+    q = torch.randn(9, 28, 128)
+    out = torch.zeros(9, 28, 128, dtype=torch.float16)
+    meta = types.SimpleNamespace(max_query_len=5, num_actual_tokens=7, causal=True,
+                                 query_start_loc=torch.tensor([0, 5, 6, 7], dtype=torch.int32),
+                                 block_table=torch.zeros((3, 6), dtype=torch.int32),
+                                 seq_lens=torch.tensor([40, 17, 90], dtype=torch.int32))
+    impl.forward(_layer(2), q, q, q, None, meta, out)
+    assert seen == [(2, (7, 28, 128), [0, 5, 6, 7], (3, 6), [40, 17, 90], 5, "physical", 0.125)]
+    assert torch.all(out[:7] == 0.25) and torch.all(out[7:] == 0) and not impl.calls
+    assert impl.forward(_layer(2), q, q, q, None, None, out) is out      # profiling run
+    w = cb.make_impl_cls(FakeImpl)(sliding_window=(511, 0))
+    with pytest.raises(NotImplementedError):
+        w.forward(_layer(2), q, q, q, None, meta, out)
+    impl.forward(_layer(2), q, q, q, None, _meta(3, 1), out)            # decode: the Quest path
+    assert [c[0] for c in calls] == ["select", "decode"]

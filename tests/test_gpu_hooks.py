@@ -168,3 +168,56 @@ def test_quantise_dequantise_hook_matches_oracle():
     vrec = np.where(vm, np16(V[:280]), vrec).astype(np.float16)
     np.testing.assert_array_equal(np16(vq[:280]).view(np.uint16), vrec.view(np.uint16))
     assert torch.equal(kq[280:], K[280:]) and torch.equal(vq[280:], V[280:])
+
+
+class FakeAttention:
+    def get_kv_cache_spec(self, vllm_config):
+        return None
+
+
+def test_compact_hook_without_fp16_cache_mixed_batch():
+    """fp16_cache=False: a mixed batch of a 40-token prefill chunk (its
+    sequence's earlier 260 tokens already in the pool) and one decode token
+    of another sequence, both served from the pool by the chunked-prefill
+    kernel; shuffled blocks, V rows by physical slot (the hook's rule)."""
+    from kvquant import compact_backend as cb
+    from kvquant.synthetic import NUQ4, make_kv, make_scales
+    H, D, S, G = 4, 128, 16, 7
+    lens, chunk = [300, 150], [40, 1]
+    sc = make_scales([NUQ4], H, D, t_cal=1024, seed=90)
+    backend = type("B", (FakeBackend,), {})
+    NB = 40
+    cb.install_compact_backend("", num_layers=1, num_blocks=NB, block_size=S, num_kv_heads=H, head_size=D,
+                               device="cuda", top_k_blocks_decode=0, scales=sc, backend_cls=backend,
+                               impl_cls=FakeImpl, fp16_cache=False, attention_cls=FakeAttention)
+    try:
+        impl = backend.get_impl_cls()(scale=D ** -0.5)
+        layer = types.SimpleNamespace(layer_name="model.layers.0.self_attn.attn")
+        g = torch.Generator(device="cuda").manual_seed(91)
+        perm = torch.randperm(NB, generator=g, device="cuda").to(torch.int32)
+        bt = torch.stack([perm[:20], perm[20:40]])                       # 20 blocks per sequence
+        orc = OraclePool(1, NB, S, H, D, oracle_scales(sc))
+        KV = [make_kv(n, H, D, seed=92 + b, chan_seed=90) for b, n in enumerate(lens)]
+        for b, n in enumerate(lens):                                     # the earlier tokens, then the chunks
+            pos = torch.arange(n, device="cuda")
+            slots = bt[b, pos // S].to(torch.int64) * S + pos % S
+            for a, e in ((0, n - chunk[b]), (n - chunk[b], n)):
+                impl.do_kv_cache_update(layer, KV[b][0][a:e], KV[b][1][a:e], None, slots[a:e])
+            orc.write_kv(0, np16(KV[b][0]), np16(KV[b][1]), np16(slots), np16(slots))
+        cb.pool().check()
+        q = torch.randn((sum(chunk), H * G, D), generator=g, device="cuda").to(torch.float16)
+        meta = types.SimpleNamespace(max_query_len=40, num_actual_tokens=41, causal=True,
+                                     query_start_loc=torch.tensor([0, 40, 41], dtype=torch.int32, device="cuda"),
+                                     block_table=bt, seq_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"))
+        out = torch.zeros((44, H * G, D), dtype=torch.float16, device="cuda")   # padded past 41 tokens
+        impl.forward(layer, torch.cat([q, q[:3]]), None, None, None, meta, out)
+        cb.pool().check()
+        assert not impl.sent and torch.all(out[41:] == 0)
+        rows = [(0, i, lens[0] - chunk[0] + i) for i in range(chunk[0])] + [(1, 40, lens[1] - 1)]
+        for b, r, pos in rows:
+            Kd, Vd = orc.dequant_sequence(0, np16(bt[b]), lens[b], v_pos="physical")
+            o, _ = oatt.decode_attention(np16(q[r]).astype(np.float64), Kd[:pos + 1], Vd[:pos + 1])
+            err = np.abs(np16(out[r]).astype(np.float64) - o)
+            assert (err <= TOL + np.abs(o) * 2.0 ** -11).all(), err.max()
+    finally:
+        cb._FP16_CACHE = True
