@@ -145,6 +145,25 @@ HX_API int hx_unpack_pages(void* stream, const hx_pool_layer* pool, const hx_lay
                            const int64_t* block_ids, const int64_t* first_pos, int32_t nk,
                            uint16_t* staging_k, uint16_t* staging_v, uint32_t* dev_err);
 
+/* ---- calibration statistics ------------------------------------------ */
+
+/* One group of samples per row: sorted (rows, n) float32, each row ascending.
+ * lower / upper (rows) receive numpy.quantile(row, q_low) / (row, q_high)
+ * (method "linear", numpy's own float32 value for float32 samples), centers
+ * (rows, k) the sorted centres of a 1-D k-means of the samples with lower <=
+ * x <= upper: the exact optimum (dynamic programming) over the samples, or
+ * over 4096 of them stratified by rank, equal values merged, then at most
+ * max_iter Lloyd steps over every band sample (a sample on a midpoint joins
+ * the lower centre); fewer samples than k: the samples and zeros, sorted.
+ * iters_done (rows, optional): the Lloyd steps run. scratch:
+ * hx_calib_scratch_bytes(rows, n) bytes. k <= 16. Replaces the statistics
+ * loop of src/kvquant/calibration.py:127-188 (there: np.quantile and
+ * sklearn's KMeans on a random subsample of 5,000). */
+HX_API int64_t hx_calib_scratch_bytes(int32_t rows, int64_t n);
+HX_API int hx_calib_rows(void* stream, const float* sorted, int32_t rows, int64_t n, double q_low,
+                         double q_high, int32_t k, int32_t max_iter, float* lower, float* upper,
+                         float* centers, double* scratch, int32_t* iters_done);
+
 /* ---- dense quantisation (the batched Triton API) ---------------------- */
 
 /* mode 0: K, poles (H, D, L), thresholds (H, D); mode 1: V, poles (H, T, L),
