@@ -504,6 +504,31 @@ class Timer:
         return statistics.median(times)
 
 
+def measure_pack(device, peak, src, tokens=CHUNK):
+    """The append as the step's pool sees it, warm: one nuq4 layer, `tokens`
+    tokens (one 64K chunk) appended in one call to whole pages; L2 flushed
+    before each call; median of 10 after 3 warm-up calls."""
+    import torch
+    from kvquant.compact_pool import CompactKVPool
+    from kvquant.synthetic import NUQ4, make_kv, make_scales
+    sc = make_scales([NUQ4], H, D, t_cal=4096, seed=700, device=device)
+    npg = tokens // S
+    pool = CompactKVPool(1, npg, S, H, D, sc, device=device, outlier_frac=0.03)
+    K, V = make_kv(tokens, H, D, seed=701, outlier_frac=0.01, device=device, chan_seed=700)
+    pos = torch.arange(tokens, device=device)
+    ms = Timer(device)(lambda: pool.write_kv(0, K, V, pos, pos))
+    pool.check()
+    lay = pool.layers[0]
+    ent = int(lay.dir[:, :, :, 2].to(torch.int64).sum())
+    b = tokens * H * D * 2 * 2 + npg * H * lay.seg + 4 * ent + npg * H * 2 * D * 2 * 2 + 4096 * H * 16 * 2
+    del pool, K, V
+    torch.cuda.empty_cache()
+    return {"value": round(b / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "tokens": tokens, "us": round(ms * 1e3, 1),
+            "what": f"nuq4 append of {tokens} tokens in one call (hx_pack_append: run pre-pass + K and V kernels), "
+                    "warm, L2 flushed before each call, median of 10",
+            "roofline": roofline(b, ms, peak, src, "pack_list_kernel<4,K|V> + pack_count_runs_kernel")}
+
+
 def run_configs(device, peak, src):
     import torch
     from kvquant import fused
@@ -994,6 +1019,15 @@ def run_ours(args):
     else:
         tot_bytes, pack_bytes, pack_tokens, pack_ms = mine, pack["bytes"], pack["tokens"], pack["ms"]
 
+    peak0, src0 = peaks()
+    pack_warm = measure_pack(device, peak0, src0)
+    if world > 1:   # every rank appends its own chunk at once: total tokens over the slowest rank
+        pv = torch.tensor([pack_warm["us"]], dtype=torch.float64, device=device)
+        dist.all_reduce(pv, op=dist.ReduceOp.MAX)
+        us = float(pv.item())
+        pack_warm["value"] = round(pack_warm["value"] * world * pack_warm["us"] / us, 2)
+        pack_warm["us"] = round(us, 1)
+        pack_warm["tokens"] *= world
     parity = None if args.no_parity else check_parity(W, args, world, rank, group)
     if graph is not None:
         del graph
@@ -1028,9 +1062,12 @@ def run_ours(args):
             "kernels": {"quest_select_ms_per_layer": round(sel_avg, 5), "decode_ms_per_layer": round(dec_avg, 5),
                         "quest_select_GBps": round(sc_b / (sel_avg * 1e-3) / 1e9, 1),
                         "decode_GBps": round(dec_b / (dec_avg * 1e-3) / 1e9, 1)},
-            "pack": {"value": round(pack_bytes / (pack_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "pack": pack_warm,
+            "build_append_one_shot": {"value": round(pack_bytes / (pack_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                      "tokens": int(pack_tokens), "ms": round(pack_ms, 3),
-                     "what": "append of the whole context for all layers, 64K-token chunks"},
+                     "what": "the pool's build: the first append of every 64K-token chunk of every layer, "
+                             "events around each call (host work and first-use preparation inside); "
+                             "informational, the warm figure is 'pack'"},
             "e2e": {"value": round(tot_bytes / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(ms_e2e, 4),
                     "how": "queries H2D from pinned host memory, the " + ("captured" if use_graph else "eager")
