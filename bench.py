@@ -66,6 +66,10 @@ def parse():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="split-KV exchange: peer-memory merge kernel, or NCCL all-gather + merge")
     ap.add_argument("--profile", action="store_true", help="setup + warmup + steps only (for ncu)")
+    ap.add_argument("--no-fused-select", action="store_true",
+                    help="keep the threshold kernel between scores and decode for small shards too")
+    ap.add_argument("--splits", type=int, default=0,
+                    help="decode splits per (sequence, KV head); 0 = about one CTA per SM")
     ap.add_argument("--decode-cores", choices=["tensor", "cuda"], default="tensor",
                     help="decode QK / PV on the tensor cores (mma.sync) or as FFMA on the CUDA cores (comparison)")
     ap.add_argument("--select", choices=["shard", "global"], default="shard",
@@ -251,7 +255,7 @@ def build_world(args, rank, world, device):
     bt = torch.arange(shard.n_pages, dtype=torch.int32, device=device).unsqueeze(0)
     sl = torch.tensor([shard.n_pages * S], dtype=torch.int32, device=device)
     kk = local_k(shard)
-    ns = fused.default_splits(1, H, shard.n_pages)
+    ns = args.splits if args.splits > 0 else fused.default_splits(1, H, shard.n_pages)
     gsel = None
     if args.select == "global" and world > 1:
         from kvquant.splitkv import GlobalSelect
@@ -289,7 +293,7 @@ def build_world(args, rank, world, device):
         pack_bytes += shard.n_pages * H * 2 * D * 2 * 2                  # stats read + written
         pack_bytes += 4 * int(lay.dir[:, :, :, 2].to(torch.int64).sum())  # outlier entries written
     return dict(pool=pool, shard=shard, qs=qs, bt=bt, sl=sl, k=kk, ns=ns, per_layer=per_layer, gsel=gsel,
-                cores=args.decode_cores,
+                cores=args.decode_cores, fused_select=not args.no_fused_select,
                 pack=dict(ms=pack_ms, tokens=pack_tokens, bytes=pack_bytes), scales=scales, layout=layout)
 
 
@@ -313,11 +317,37 @@ def make_step(W, world, group, timing=None):
     pex = W.get("pex")
     ex = Exchange(H * G, D, world, dev, group) if world > 1 and pex is None else None
 
+    # rows of at most FUSED_MAX_PAGES pages (N >= 4 at 1M): the decode's CTAs
+    # find the threshold themselves, no threshold kernel between scores and decode
+    fused_sel = W.get("gsel") is None and shard.n_pages <= fused.FUSED_MAX_PAGES and W.get("fused_select", True)
+    hist = hxlib.scratch(dev, "quest_hist", H * 2 * 4096 * 4)
+
     def step(q_in=None):
         q_all = qs if q_in is None else q_in
         for li in range(L):
             if timing is not None:
                 timing["ev"][li][0].record()
+            if fused_sel:
+                fused.page_scores(pool, li, q_all[li], bt, sl, shard.n_pages, shard.sink_pages, scores[li], hist)
+                if timing is not None:
+                    timing["ev"][li][1].record()
+                if world == 1:
+                    o_dst, lse_dst = o_out[li].view(1, H * G, D), lse_loc[li]
+                elif pex is not None:
+                    o_dst, lse_dst = pex.o_view(li).view(1, H * G, D), pex.lse_view(li).view(1, H * G)
+                else:
+                    o_dst, lse_dst = o_loc[li], lse_loc[li]
+                fused.decode_select(pool, li, q_all[li], bt, sl, scores[li], top_k=W["k"],
+                                    sink_pages=shard.sink_pages, page_begin=shard.page_begin, n_splits=W["ns"],
+                                    o=o_dst, lse=lse_dst, cores=W.get("cores", "tensor"))
+                if timing is not None:
+                    timing["ev"][li][2].record()
+                if world > 1:
+                    if pex is not None:
+                        pex.merge(li, o_out[li])
+                    else:
+                        ex.merge(o_loc[li].view(H * G, D), lse_loc[li].view(H * G), o_out[li])
+                continue
             if W.get("gsel") is not None:
                 sel = W["gsel"].select(pool, li, q_all[li], bt, sl, shard)
             else:
@@ -1056,6 +1086,9 @@ def run_ours(args):
             "config": workload(args, world),
             "run": {"cuda_graph": use_graph, "n_splits_per_head": W["ns"], "steps_replayed": args.steps,
                     "exchange": exchange, "decode_cores": W["cores"],
+                    "selection_kernels": ("scores + decode (threshold inside the decode)"
+                                          if W.get("gsel") is None and W["fused_select"]
+                                          and W["shard"].n_pages <= 16384 else "scores + threshold + decode"),
                     "selection": ("top-K of the whole sequence (one GPU's)" if world == 1 or W.get("gsel") is not None
                                   else "top-K of each shard's pages")},
             "roofline": roofline(dom_b, dom_ms, peak, peak_src, dom, read_traffic(dom)),

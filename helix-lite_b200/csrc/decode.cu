@@ -22,6 +22,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "select.cuh"
 
 namespace hx {
 
@@ -48,6 +49,13 @@ struct DecodeParams {
   int page_begin, max_pages, sel_mode;
   int vphys;  // V positions from the physical page (HX_VPOS_PHYSICAL)
   int cores;  // QK and PV on CUDA cores (HX_DECODE_CUDA_CORES)
+  // fused selection (hx_decode_attn_select): each CTA finds its row's
+  // threshold and slice counts from the scores and the level-1 histogram
+  int fsel;
+  uint32_t* fhist;
+  int k_fixed, fnum, fden;
+  uint64_t* thresh_out;
+  int32_t* slice_out;
   const float* scores;
   const uint64_t* thresh;
   int sinks_req;
@@ -289,7 +297,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   if (tid < NLV) sm.vtail[tid] = vtail_level(tid);
   if (BV == 2 && tid >= 32 && tid < 48) sm.vpair[tid - 32] = pack_u16x2(vtail_level((tid - 32) & 3), vtail_level((tid - 32) >> 2));
   WarpSmem& ws = sm.w[warp];
-  if (lane == 0) {
+  if (lane == 0 && !p.fsel) {  // fused selection: after the selection, whose scratch they share
     for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
     fence_mbar_init();
   }
@@ -298,11 +306,61 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   pdl_wait();
   const int seq_len = p.seq_lens[b];
   const int n = min((seq_len + DS - 1) / DS, p.max_pages);
+  // fused selection: the row's exact threshold and the exclusive prefix of
+  // its slices' selected counts, computed here by every CTA of the row (the
+  // warp buffers are its scratch; the mbarriers are set up afterwards)
+  __shared__ int32_t s_soff[fsel::kMaxSlices + 1];
+  uint64_t T_f = 0ull;
+  if (p.fsel) {
+    fsel::RowSel<NT>& rs = *reinterpret_cast<fsel::RowSel<NT>*>(sm.w);
+    const int fs = min(max(p.sinks_req, 0), n);
+    const long long kb = p.fden > 0 ? (long long)n * p.fnum / p.fden : (long long)p.k_fixed;
+    const long long ke = kb < (long long)(n - fs) ? kb : (long long)(n - fs);
+    const int C = p.list_stride - 1;
+    T_f = fsel::row_select<NT>(p.scores + (int64_t)bh * p.max_pages, p.fhist + (int64_t)bh * 2 * fsel::kBins, n, fs,
+                               (int)(ke > 0 ? ke : 0), C, rs, p.err);
+    if (tid < 32) {  // exclusive prefix of the C <= 128 slice counts (one warp)
+      uint32_t v[fsel::kMaxSlices / 32];
+      uint32_t sum = 0;
+#pragma unroll
+      for (int q = 0; q < fsel::kMaxSlices / 32; ++q) {
+        const int i = (fsel::kMaxSlices / 32) * lane + q;
+        v[q] = i < C ? rs.add[i] : 0u;
+        sum += v[q];
+      }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += x;
+      }
+      uint32_t acc = incl - sum;
+#pragma unroll
+      for (int q = 0; q < fsel::kMaxSlices / 32; ++q) {
+        const int i = (fsel::kMaxSlices / 32) * lane + q;
+        if (i < C) s_soff[i] = (int32_t)acc;
+        acc += v[q];
+      }
+      if (lane == 31) s_soff[C] = (int32_t)incl;
+    }
+    __syncthreads();
+    if (split == 0) {
+      if (tid == 0 && p.thresh_out) p.thresh_out[bh] = T_f;
+      if (p.slice_out)
+        for (int i = tid; i <= C; i += NT) p.slice_out[(int64_t)bh * (C + 1) + i] = s_soff[i];
+    }
+    __syncthreads();  // the scratch is free: the warps' mbarriers now
+    if (lane == 0) {
+      for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+  }
   // HX_SEL_SLICES: the row's slice offsets (exclusive selected counts of the
   // slices of the non-sink pages)
   const bool slices = p.sel_mode == HX_SEL_SLICES;
   const int nsl = slices ? p.list_stride - 1 : 1;
-  const int32_t* soff = slices ? p.lists + (int64_t)bh * p.list_stride : nullptr;
+  const int32_t* soff = slices ? (p.fsel ? s_soff : p.lists + (int64_t)bh * p.list_stride) : nullptr;
   const int32_t soff_lo = (slices && tid < nsl) ? soff[tid] : 0, soff_hi = (slices && tid < nsl) ? soff[tid + 1] : 0;
   const int32_t soff_all = slices ? soff[nsl] : 0;
 
@@ -366,7 +424,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   else total = n;
   const int per = (total + p.n_splits - 1) / p.n_splits;
   const int ra = min(split * per, total), re = min(ra + per, total);
-  const uint64_t T = (p.sel_mode == HX_SEL_THRESHOLD || slices) ? p.thresh[bh] : 0ull;
+  const uint64_t T = p.fsel ? T_f : ((p.sel_mode == HX_SEL_THRESHOLD || slices) ? p.thresh[bh] : 0ull);
   int j_cur = -1, r_cur = 0;  // HX_SEL_SLICES scan cursor: page, non-sink rank of the next selected page
   const float* sc_bh = p.scores ? p.scores + (int64_t)bh * p.max_pages : nullptr;
   // a page whose 16 tokens all lie before t_cal gets its per-token V levels by
@@ -876,6 +934,10 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
+  // every CTA of the row is past its selection: leave the row's level-1
+  // histogram zero for the next scoring
+  if (p.fsel)
+    for (int i = tid; i < fsel::kBins; i += NT) p.fhist[(int64_t)bh * 2 * fsel::kBins + i] = 0u;
 
   // ---- last CTA of (b, h): merge the splits
   __syncthreads();  // every thread is past its reads of the warp buffers
@@ -1160,6 +1222,11 @@ static int prepare_decode(DecodeParams& p, const hx_pool_layer* pool, const hx_l
   p.err = dev_err;
   p.ctr = nullptr;
   p.part = nullptr;
+  p.fsel = 0;
+  p.fhist = nullptr;
+  p.k_fixed = p.fnum = p.fden = 0;
+  p.thresh_out = nullptr;
+  p.slice_out = nullptr;
   return HX_OK;
 }
 
@@ -1177,6 +1244,37 @@ static int launch_prepared(DecodeParams& p, void* scratch, cudaStream_t s) {
   if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2, false>(p, H, s);
   if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4, false>(p, H, s);
   return launch_decode<2, 2, false>(p, H, s);
+}
+
+HX_API int hx_decode_attn_select(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
+                                 const uint16_t* q, int32_t B, int32_t group, float softmax_scale,
+                                 const int32_t* block_table, int32_t bt_stride, const int32_t* seq_lens,
+                                 int32_t page_begin, int32_t max_pages, int32_t flags, const float* scores,
+                                 uint32_t* hist, int32_t sink_pages, int32_t k_fixed, int32_t frac_num,
+                                 int32_t frac_den, int32_t n_splits, void* scratch, float* o, float* lse,
+                                 uint16_t* out16, uint64_t* thresh_out, int32_t* slice_out, uint32_t* dev_err) {
+  if ((flags & ~(HX_VPOS_PHYSICAL | HX_DECODE_CUDA_CORES)) != 0) return HX_ERR_ARG;
+  if (!scores || !hist || k_fixed < 0 || frac_num < 0 || frac_den < 0) return HX_ERR_ARG;
+  if (max_pages > fsel::kFusedMaxPages) return HX_ERR_UNSUPPORTED;
+  DecodeParams p;
+  const int rc = prepare_decode(p, pool, sc, q, B, group, softmax_scale, block_table, bt_stride, seq_lens, page_begin,
+                                max_pages, HX_SEL_DENSE | flags, scores, nullptr, sink_pages, nullptr, 0, nullptr,
+                                n_splits, o, lse, out16, dev_err);
+  if (rc != HX_OK) return rc;
+  if (!scratch) return HX_ERR_ARG;
+  if (B == 0) return HX_OK;
+  const int C = hx_quest_slices(max_pages);
+  if (C < 1 || C > fsel::kMaxSlices) return HX_ERR_UNSUPPORTED;
+  p.sel_mode = HX_SEL_SLICES;
+  p.fsel = 1;
+  p.fhist = hist;
+  p.k_fixed = k_fixed;
+  p.fnum = frac_num;
+  p.fden = frac_den;
+  p.list_stride = C + 1;
+  p.thresh_out = thresh_out;
+  p.slice_out = slice_out;
+  return launch_prepared(p, scratch, S_(stream));
 }
 
 HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc, const uint16_t* q,

@@ -73,6 +73,9 @@ _SIGS = {
     "hx_calib_scratch_bytes": (c_i64, [c_i32, c_i64]),
     "hx_calib_rows": (c_i32, [c_vp, c_vp, c_i32, c_i64, ctypes.c_double, ctypes.c_double, c_i32, c_i32, c_vp, c_vp,
                               c_vp, c_vp, c_vp]),
+    "hx_decode_attn_select": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_i32, c_i32, c_f32, c_vp, c_i32,
+                                      c_vp, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32,
+                                      c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "hx_prefill_attn": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_vp, c_i32, c_i32, c_f32, c_vp, c_i32,
                                 c_vp, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp]),
     "hx_decode_attn_noalloc": (c_i32, [c_vp, _P(PoolLayer), _P(LayerScales), c_vp, c_i32, c_i32, c_f32, c_vp,
@@ -119,7 +122,7 @@ LAUNCHES = {"hx_scales_prepare": 2, "hx_pool_init": 1, "hx_pool_reset_pages": 1,
             "hx_nuq_pack_dense": 1, "hx_nuq_unpack_dense": 1, "hx_nuq_quantize_flat": 2,
             "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": lambda a: 1 if a[11] else 2,
             "hx_quest_threshold_slices": lambda a: 1 if a[11] else 2, "hx_quest_localize": 1,
-            "hx_quest_compact": 1, "hx_quest_lists": 2, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_prefill_attn": 1, "hx_calib_rows": 1, "hx_merge_partials": 1, "hx_merge_gathered": 1, "hx_exchange_merge": 1,
+            "hx_quest_compact": 1, "hx_quest_lists": 2, "hx_decode_attn": 1, "hx_decode_attn_noalloc": 1, "hx_prefill_attn": 1, "hx_calib_rows": 1, "hx_decode_attn_select": 1, "hx_merge_partials": 1, "hx_merge_gathered": 1, "hx_exchange_merge": 1,
             "hx_selected_attention": 1}
 launch_count = [0]
 

@@ -231,6 +231,74 @@ def decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table
     return o, lse
 
 
+FUSED_MAX_PAGES = 16384   # rows the decode can select for itself (hx_decode_attn_select)
+
+
+def quest_decode(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, block_table: torch.Tensor,
+                 seq_lens: torch.Tensor, *, top_k: int | None = None, top_frac=(1, 4), sink_pages: int = 4,
+                 gqa: str = "sum", max_pages: int | None = None, scores: torch.Tensor | None = None, **kw):
+    """Quest selection and fused decode in two kernels: the page scores (with
+    their level-1 histogram), then the decode, whose CTAs find their row's
+    exact top-K threshold themselves (hx_decode_attn_select). Same selection
+    and outputs as quest_select + decode, without the threshold kernel; rows
+    of at most FUSED_MAX_PAGES pages. Keyword arguments of decode_select
+    pass through. Returns (o, lse)."""
+    dev = pool.device
+    q = query.to(device=dev, dtype=torch.float16).contiguous()
+    B, Hq, D = q.shape
+    H = pool.num_kv_heads
+    if Hq % H:
+        raise ValueError("query heads must be a multiple of KV heads")
+    bt = _i32(block_table, dev)
+    sl = _i32(seq_lens, dev)
+    mp = int(max_pages if max_pages is not None else bt.shape[1])
+    if scores is None:
+        scores = torch.empty((B, H, max(mp, 1)), dtype=torch.float32, device=dev)
+    hist = hxlib.scratch(dev, "quest_hist", B * H * 2 * 4096 * 4)
+    with torch.cuda.device(dev):
+        page_scores(pool, layer_idx, q, bt, sl, mp, sink_pages, scores, hist, gqa)
+    return decode_select(pool, layer_idx, q, bt, sl, scores, top_k=top_k, top_frac=top_frac, sink_pages=sink_pages,
+                         max_pages=mp, **kw)
+
+
+def decode_select(pool: CompactKVPool, layer_idx: int, q: torch.Tensor, bt: torch.Tensor, sl: torch.Tensor,
+                  scores: torch.Tensor, *, top_k: int | None = None, top_frac=(1, 4), sink_pages: int = 4,
+                  max_pages: int | None = None, page_begin: int = 0, n_splits: int | None = None,
+                  softmax_scale: float | None = None, o: torch.Tensor | None = None,
+                  lse: torch.Tensor | None = None, out16: torch.Tensor | None = None, v_pos: str = "logical",
+                  cores: str = "tensor", thresh_out: torch.Tensor | None = None,
+                  slice_out: torch.Tensor | None = None):
+    """The decode half of quest_decode: ``scores`` and the level-1 histogram
+    (the "quest_hist" scratch) from page_scores; q fp16, bt / sl int32 on the
+    pool's device. thresh_out (B*H,) int64 and slice_out (B*H, slices + 1)
+    int32 receive the rows' thresholds and slice offsets when given."""
+    dev = pool.device
+    B, Hq, D = q.shape
+    H = pool.num_kv_heads
+    if cores not in ("tensor", "cuda"):
+        raise ValueError("cores must be 'tensor' or 'cuda'")
+    mp = int(max_pages if max_pages is not None else bt.shape[1])
+    if mp > FUSED_MAX_PAGES:
+        raise ValueError(f"decode_select selects rows of at most {FUSED_MAX_PAGES} pages; use quest_select")
+    hist = hxlib.scratch(dev, "quest_hist", B * H * 2 * 4096 * 4)
+    kf, fn, fd = (int(top_k), 0, 0) if top_k is not None else (0, int(top_frac[0]), int(top_frac[1]))
+    ns = int(n_splits or default_splits(B, H, mp))
+    scale = float(softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D))
+    if o is None:
+        o = torch.empty((B, Hq, D), dtype=torch.float32, device=dev)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=dev)
+    scr = hxlib.scratch(dev, "decode", hxlib.lib().hx_decode_scratch_bytes(B, H, ns))
+    st_scales, _keep = pool.scales.device_layer(layer_idx, dev)
+    flags = (hxlib.VPOS_PHYSICAL if v_pos == "physical" else 0) | (hxlib.DECODE_CUDA_CORES if cores == "cuda" else 0)
+    with torch.cuda.device(dev):
+        call("hx_decode_attn_select", stream(dev), ctypes_ref(pool.layers[layer_idx].struct), ctypes_ref(st_scales),
+             ptr(q), B, Hq // H, scale, ptr(bt), bt.shape[1], ptr(sl), int(page_begin), mp, flags, ptr(scores),
+             ptr(hist), sink_pages, kf, fn, fd, ns, ptr(scr), ptr(o), ptr(lse), ptr(out16), ptr(thresh_out),
+             ptr(slice_out), ptr(hxlib.err_word(dev)))
+    return o, lse
+
+
 def prefill(pool: CompactKVPool, layer_idx: int, query: torch.Tensor, query_start: torch.Tensor,
             block_table: torch.Tensor, seq_lens: torch.Tensor, *, max_query_len: int | None = None,
             softmax_scale: float | None = None, v_pos: str = "logical", out: torch.Tensor | None = None,

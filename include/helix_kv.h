@@ -354,6 +354,30 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
                           uint32_t* dev_err);
 
 /*
+ * Quest selection and decode in one kernel, for rows of at most 16384 pages
+ * (split-KV shards, batched sequences): hx_decode_attn in HX_SEL_SLICES mode
+ * whose CTAs each compute their row's exact threshold and slice counts from
+ * `scores` and the level-1 histogram `hist` that hx_quest_scores wrote (the
+ * work of hx_quest_threshold_slices, same selection: k_b = frac_den > 0 ?
+ * n_b*frac_num/frac_den : k_fixed, sinks forced, ties to the lower page), so
+ * the threshold kernel and its chain of global round trips go away. The
+ * row's last CTA leaves its histogram zero for the next scoring. flags:
+ * HX_VPOS_PHYSICAL, HX_DECODE_CUDA_CORES. thresh_out (B*H) and slice_out
+ * (B*H, hx_quest_slices(max_pages) + 1), when non-NULL, receive the row's
+ * threshold and slice offsets. max_pages > 16384: HX_ERR_UNSUPPORTED.
+ * Replaces select_top_blocks_for_layer + unpack_to_staging + FlashAttention
+ * in KVQuantCompactImpl.forward (compact_backend.py:225-299).
+ */
+HX_API int hx_decode_attn_select(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,
+                                 const uint16_t* q, int32_t B, int32_t group, float softmax_scale,
+                                 const int32_t* block_table, int32_t bt_stride, const int32_t* seq_lens,
+                                 int32_t page_begin, int32_t max_pages, int32_t flags,
+                                 const float* scores, uint32_t* hist, int32_t sink_pages,
+                                 int32_t k_fixed, int32_t frac_num, int32_t frac_den, int32_t n_splits,
+                                 void* scratch, float* o, float* lse, uint16_t* out16,
+                                 uint64_t* thresh_out, int32_t* slice_out, uint32_t* dev_err);
+
+/*
  * Chunked-prefill attention over the compact pool. q (Tq, H*group, D) fp16
  * holds B sequences' query tokens back to back: sequence b's are rows
  * q_start[b] .. q_start[b+1] - 1 (q_start (B+1) int32, device), the last

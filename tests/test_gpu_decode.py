@@ -283,3 +283,48 @@ def test_decode_slice_counts_match_lists(k, n_splits):
     pages = [[lists[b * 4 + h, :counts[b * 4 + h]] for h in range(4)] for b in range(len(lens))]
     ro, _ = _oracle_out(orc, 0, q, bt, sl, pages)
     assert np.abs(np16(o_s) - ro).max() < TOL
+
+
+@pytest.mark.parametrize("case", ["config3", "ragged", "ties", "edges"])
+def test_fused_selection_decode_equals_two_kernel_path(case):
+    """hx_decode_attn_select (each CTA finds its row's threshold) against
+    quest_select + decode: the same thresholds' selections, the same slice
+    offsets and the same outputs, bit for bit; the histogram is left zero."""
+    import hxlib
+    from kvquant import fused
+    from kvquant.synthetic import NUQ2, NUQ4
+    if case == "config3":
+        gpu, orc, bt, sl = _build([NUQ4], [16384], seed=130)
+        kw = dict(top_frac=(1, 4), sink_pages=4)
+    elif case == "ragged":
+        gpu, orc, bt, sl = _build([NUQ2], [1, 16, 777, 5000, 2048 + 5], seed=131, B=5, shuffle=True, pages_extra=3)
+        kw = dict(top_frac=(1, 4), sink_pages=4)
+    elif case == "ties":     # all-equal page statistics: ties everywhere
+        gpu, orc, bt, sl = _build([NUQ4], [4000], seed=132)
+        gpu.layers[0].stats.zero_()
+        kw = dict(top_k=300, sink_pages=4)
+    else:                    # k = 0 and k beyond the pages
+        gpu, orc, bt, sl = _build([NUQ4], [3000, 500], seed=133, B=2)
+        kw = dict(top_k=0, sink_pages=2)
+    B = bt.shape[0]
+    q = _query(B, 7, 134)
+    ns = 6
+    for kw2 in ([kw] if case != "edges" else [kw, dict(top_k=10 ** 6, sink_pages=2)]):
+        sel = fused.quest_select(gpu, 0, q, bt, sl, **kw2)
+        o_ref, l_ref = fused.decode(gpu, 0, q, bt, sl, sel, n_splits=ns)
+        H = gpu.num_kv_heads
+        C = int(hxlib.lib().hx_quest_slices(bt.shape[1]))
+        th = torch.empty((B * H,), dtype=torch.int64, device="cuda")
+        so = torch.empty((B * H, C + 1), dtype=torch.int32, device="cuda")
+        o, l_ = fused.quest_decode(gpu, 0, q, bt, sl, n_splits=ns, thresh_out=th, slice_out=so, **kw2)
+        gpu.check()
+        np.testing.assert_array_equal(np16(so), np16(sel.slice_off))
+        lists, counts = fused.selected_lists(sel)
+        sel2 = fused.Selection(sel.scores, th, sel.seq_lens, sel.page_size, sel.max_pages, sel.sink_pages)
+        lists2, counts2 = fused.selected_lists(sel2)
+        np.testing.assert_array_equal(np16(counts2), np16(counts))
+        np.testing.assert_array_equal(np16(lists2), np16(lists))
+        np.testing.assert_array_equal(np16(o), np16(o_ref))
+        np.testing.assert_array_equal(np16(l_), np16(l_ref))
+        hist = hxlib.scratch("cuda", "quest_hist", 4)
+        assert int(hist.view(torch.int32)[:B * H * 2 * 4096].abs().sum()) == 0
