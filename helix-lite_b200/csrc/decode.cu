@@ -235,7 +235,9 @@ HX_DEVINL uint32_t stage_v(uint32_t ek, uint32_t cntv) { return min((cntv + 3u) 
 
 // FMA: QK and PV in fp32 FFMA on the CUDA cores instead of mma.sync (the
 // same pipeline, dequant, tile and softmax state; the comparison variant).
-template <int BK, int BV, bool FMA>
+// FSEL: the fused selection (hx_decode_attn_select) compiled in; the other
+// instances carry none of its code.
+template <int BK, int BV, bool FMA, bool FSEL>
 __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   CtaSmem& sm = *reinterpret_cast<CtaSmem*>(smem_raw);
@@ -297,7 +299,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   if (tid < NLV) sm.vtail[tid] = vtail_level(tid);
   if (BV == 2 && tid >= 32 && tid < 48) sm.vpair[tid - 32] = pack_u16x2(vtail_level((tid - 32) & 3), vtail_level((tid - 32) >> 2));
   WarpSmem& ws = sm.w[warp];
-  if (lane == 0 && !p.fsel) {  // fused selection: after the selection, whose scratch they share
+  if (lane == 0 && !FSEL) {  // fused selection: after the selection, whose scratch they share
     for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
     fence_mbar_init();
   }
@@ -309,9 +311,9 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   // fused selection: the row's exact threshold and the exclusive prefix of
   // its slices' selected counts, computed here by every CTA of the row (the
   // warp buffers are its scratch; the mbarriers are set up afterwards)
-  __shared__ int32_t s_soff[fsel::kMaxSlices + 1];
+  __shared__ int32_t s_soff[FSEL ? fsel::kMaxSlices + 1 : 1];
   uint64_t T_f = 0ull;
-  if (p.fsel) {
+  if constexpr (FSEL) {
     fsel::RowSel<NT>& rs = *reinterpret_cast<fsel::RowSel<NT>*>(sm.w);
     const int fs = min(max(p.sinks_req, 0), n);
     const long long kb = p.fden > 0 ? (long long)n * p.fnum / p.fden : (long long)p.k_fixed;
@@ -360,7 +362,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   // slices of the non-sink pages)
   const bool slices = p.sel_mode == HX_SEL_SLICES;
   const int nsl = slices ? p.list_stride - 1 : 1;
-  const int32_t* soff = slices ? (p.fsel ? s_soff : p.lists + (int64_t)bh * p.list_stride) : nullptr;
+  const int32_t* soff = slices ? (FSEL ? s_soff : p.lists + (int64_t)bh * p.list_stride) : nullptr;
   const int32_t soff_lo = (slices && tid < nsl) ? soff[tid] : 0, soff_hi = (slices && tid < nsl) ? soff[tid + 1] : 0;
   const int32_t soff_all = slices ? soff[nsl] : 0;
 
@@ -424,7 +426,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   else total = n;
   const int per = (total + p.n_splits - 1) / p.n_splits;
   const int ra = min(split * per, total), re = min(ra + per, total);
-  const uint64_t T = p.fsel ? T_f : ((p.sel_mode == HX_SEL_THRESHOLD || slices) ? p.thresh[bh] : 0ull);
+  const uint64_t T = FSEL ? T_f : ((p.sel_mode == HX_SEL_THRESHOLD || slices) ? p.thresh[bh] : 0ull);
   int j_cur = -1, r_cur = 0;  // HX_SEL_SLICES scan cursor: page, non-sink rank of the next selected page
   const float* sc_bh = p.scores ? p.scores + (int64_t)bh * p.max_pages : nullptr;
   // a page whose 16 tokens all lie before t_cal gets its per-token V levels by
@@ -936,7 +938,7 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   __threadfence();
   // every CTA of the row is past its selection: leave the row's level-1
   // histogram zero for the next scoring
-  if (p.fsel)
+  if constexpr (FSEL)
     for (int i = tid; i < fsel::kBins; i += NT) p.fhist[(int64_t)bh * 2 * fsel::kBins + i] = 0u;
 
   // ---- last CTA of (b, h): merge the splits
@@ -1128,7 +1130,7 @@ using namespace hx;
 
 static inline cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-template <int BK, int BV, bool FMA>
+template <int BK, int BV, bool FMA, bool FSEL>
 static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
   const size_t smem = sizeof(CtaSmem);
   // per device, once: the attribute call is idempotent, so two threads that
@@ -1137,13 +1139,13 @@ static int launch_decode(const DecodeParams& p, int H, cudaStream_t s) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_ERR_LAUNCH;
   if (!attr_set[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(decode_kernel<BK, BV, FMA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(decode_kernel<BK, BV, FMA, FSEL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
       return HX_ERR_LAUNCH;
     attr_set[dev].store(true, std::memory_order_release);
   }
   dim3 grid(p.n_splits, H, p.B);
-  if (hx_launch_pdl(decode_kernel<BK, BV, FMA>, grid, dim3(NT), smem, s, p) != cudaSuccess) {
+  if (hx_launch_pdl(decode_kernel<BK, BV, FMA, FSEL>, grid, dim3(NT), smem, s, p) != cudaSuccess) {
     (void)cudaGetLastError();
     return HX_ERR_LAUNCH;
   }
@@ -1234,16 +1236,23 @@ static int launch_prepared(DecodeParams& p, void* scratch, cudaStream_t s) {
   p.ctr = reinterpret_cast<uint32_t*>(scratch);
   p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCtrBytes);
   const int H = p.pool.num_kv_heads;
+  if (p.cores && p.fsel) return HX_ERR_UNSUPPORTED;  // the CUDA-core comparison runs with the threshold kernel
   if (p.cores) {
-    if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4, true>(p, H, s);
-    if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2, true>(p, H, s);
-    if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4, true>(p, H, s);
-    return launch_decode<2, 2, true>(p, H, s);
+    if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4, true, false>(p, H, s);
+    if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2, true, false>(p, H, s);
+    if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4, true, false>(p, H, s);
+    return launch_decode<2, 2, true, false>(p, H, s);
   }
-  if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4, false>(p, H, s);
-  if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2, false>(p, H, s);
-  if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4, false>(p, H, s);
-  return launch_decode<2, 2, false>(p, H, s);
+  if (p.fsel) {
+    if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4, false, true>(p, H, s);
+    if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2, false, true>(p, H, s);
+    if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4, false, true>(p, H, s);
+    return launch_decode<2, 2, false, true>(p, H, s);
+  }
+  if (p.pool.bits_k == 4 && p.pool.bits_v == 4) return launch_decode<4, 4, false, false>(p, H, s);
+  if (p.pool.bits_k == 4 && p.pool.bits_v == 2) return launch_decode<4, 2, false, false>(p, H, s);
+  if (p.pool.bits_k == 2 && p.pool.bits_v == 4) return launch_decode<2, 4, false, false>(p, H, s);
+  return launch_decode<2, 2, false, false>(p, H, s);
 }
 
 HX_API int hx_decode_attn_select(void* stream, const hx_pool_layer* pool, const hx_layer_scales* sc,

@@ -362,7 +362,8 @@ HX_API int hx_decode_attn(void* stream, const hx_pool_layer* pool, const hx_laye
  * n_b*frac_num/frac_den : k_fixed, sinks forced, ties to the lower page), so
  * the threshold kernel and its chain of global round trips go away. The
  * row's last CTA leaves its histogram zero for the next scoring. flags:
- * HX_VPOS_PHYSICAL, HX_DECODE_CUDA_CORES. thresh_out (B*H) and slice_out
+ * HX_VPOS_PHYSICAL (HX_DECODE_CUDA_CORES: HX_ERR_UNSUPPORTED, the CUDA-core
+ * comparison runs with the threshold kernel). thresh_out (B*H) and slice_out
  * (B*H, hx_quest_slices(max_pages) + 1), when non-NULL, receive the row's
  * threshold and slice offsets. max_pages > 16384: HX_ERR_UNSUPPORTED.
  * Replaces select_top_blocks_for_layer + unpack_to_staging + FlashAttention
