@@ -556,7 +556,7 @@ def measure_pack(device, peak, src, tokens=CHUNK):
     return {"value": round(b / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "tokens": tokens, "us": round(ms * 1e3, 1),
             "what": f"nuq4 append of {tokens} tokens in one call (hx_pack_append: run pre-pass + K and V kernels), "
                     "warm, L2 flushed before each call, median of 10",
-            "roofline": roofline(b, ms, peak, src, "pack_list_kernel<4,K|V> + pack_count_runs_kernel")}
+            "roofline": roofline(b, ms, peak, src, "pack_kv_kernel<4,4> + pack_count_runs_kernel")}
 
 
 def run_configs(device, peak, src):
@@ -591,7 +591,7 @@ def run_configs(device, peak, src):
         "pack_us": round(pack_ms * 1e3, 2), "pack_GBps": round(pack_b / (pack_ms * 1e-3) / 1e9, 1),
         "unpack_us": round(unpack_ms * 1e3, 2), "unpack_GBps": round(unpack_b / (unpack_ms * 1e-3) / 1e9, 1),
         "roundtrip_us": round((pack_ms + unpack_ms) * 1e3, 2),
-        "roofline": roofline(pack_b, pack_ms, peak, src, "pack_fast_kernel"),
+        "roofline": roofline(pack_b, pack_ms, peak, src, "pack_kv_kernel<4,4> + pack_count_runs_kernel"),
         "note": "8 MB of input: one launch is latency-bound at this size (config 4 is the bandwidth case)"}
     del pool, K, V, sk, sv
 
@@ -746,7 +746,7 @@ def run_configs(device, peak, src):
                 "(append + Quest 25% + 4 sinks + fused decode); L2 flushed before each call",
         "append_us": round(append_ms * 1e3, 1), "append_GBps": round(append_b / (append_ms * 1e-3) / 1e9, 1),
         "decode_step_us": round(dec_ms * 1e3, 1), "decode_GBps": round(dec_b / (dec_ms * 1e-3) / 1e9, 1),
-        "roofline": roofline(append_b, append_ms, peak, src, "pack_fast_kernel<4,4>")}
+        "roofline": roofline(append_b, append_ms, peak, src, "pack_kv_kernel<4,4> + pack_count_runs_kernel")}
     del pool, Kc, Vc
     torch.cuda.empty_cache()
     return out

@@ -974,49 +974,59 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
     }
   }
   __syncthreads();
-  for (int i = tid; i < G * (DD / 4); i += NT) {
-    const int c = i / (DD / 4), d4 = i % (DD / 4);
-    // eight splits' partials in flight per pass, four accumulators
-    float4 acc[4];
+  {
+    // two threads per (column, 4 channels): even and odd splits, eight
+    // partials in flight per pass, then one shuffle adds the halves
+    // (G * DD / 4 <= 256 groups: one pass of the block covers them all)
+    const int item = tid >> 1, half = tid & 1;
+    const bool active = item < G * (DD / 4);
+    const int c = active ? item / (DD / 4) : 0, d4 = item % (DD / 4);
+    float4 acc[2];
+    acc[0] = acc[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (active) {
+      int s = half;
+      for (; s + 14 < p.n_splits; s += 16) {
+        float4 v[8];
 #pragma unroll
-    for (int a4 = 0; a4 < 4; ++a4) acc[a4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    int s = 0;
-    for (; s + 8 <= p.n_splits; s += 8) {
-      float4 v[8];
+        for (int u = 0; u < 8; ++u)
+          v[u] = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)(s + 2 * u) * PSZ + c * DD) + d4);
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        v[u] = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)(s + u) * PSZ + c * DD) + d4);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float w = wts[(s + u) * 8 + c];
-        acc[u & 3].x += w * v[u].x; acc[u & 3].y += w * v[u].y;
-        acc[u & 3].z += w * v[u].z; acc[u & 3].w += w * v[u].w;
+        for (int u = 0; u < 8; ++u) {
+          const float w = wts[(s + 2 * u) * 8 + c];
+          acc[u & 1].x += w * v[u].x; acc[u & 1].y += w * v[u].y;
+          acc[u & 1].z += w * v[u].z; acc[u & 1].w += w * v[u].w;
+        }
+      }
+      for (; s < p.n_splits; s += 2) {
+        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)s * PSZ + c * DD) + d4);
+        const float w0 = wts[s * 8 + c];
+        acc[0].x += w0 * v0.x; acc[0].y += w0 * v0.y; acc[0].z += w0 * v0.z; acc[0].w += w0 * v0.w;
       }
     }
-    for (; s < p.n_splits; ++s) {
-      const float4 v0 = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)s * PSZ + c * DD) + d4);
-      const float w0 = wts[s * 8 + c];
-      acc[0].x += w0 * v0.x; acc[0].y += w0 * v0.y; acc[0].z += w0 * v0.z; acc[0].w += w0 * v0.w;
-    }
-    const float4 A = make_float4(acc[0].x + acc[2].x, acc[0].y + acc[2].y, acc[0].z + acc[2].z, acc[0].w + acc[2].w);
-    const float4 Bv = make_float4(acc[1].x + acc[3].x, acc[1].y + acc[3].y, acc[1].z + acc[3].z, acc[1].w + acc[3].w);
-    const float L = sm.colL[c];
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    const float4 ov = make_float4((A.x + Bv.x) * inv, (A.y + Bv.y) * inv, (A.z + Bv.z) * inv, (A.w + Bv.w) * inv);
-    const int64_t row = (int64_t)b * H * G + (int64_t)h * G + c;
-    float* orow = p.o + row * DD + 4 * d4;
-    if ((reinterpret_cast<uintptr_t>(p.o) & 15u) == 0) {
-      *reinterpret_cast<float4*>(orow) = ov;
-    } else {
-      orow[0] = ov.x; orow[1] = ov.y; orow[2] = ov.z; orow[3] = ov.w;
-    }
-    if (p.out16) {
-      uint16_t* hrow = p.out16 + row * DD + 4 * d4;
-      hrow[0] = f2h(ov.x); hrow[1] = f2h(ov.y); hrow[2] = f2h(ov.z); hrow[3] = f2h(ov.w);
-    }
-    if (d4 == 0) {
-      const float M = sm.colM[c];
-      p.lse[row] = L > 0.0f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+    float4 A = make_float4(acc[0].x + acc[1].x, acc[0].y + acc[1].y, acc[0].z + acc[1].z, acc[0].w + acc[1].w);
+    A.x += __shfl_xor_sync(0xffffffffu, A.x, 1);
+    A.y += __shfl_xor_sync(0xffffffffu, A.y, 1);
+    A.z += __shfl_xor_sync(0xffffffffu, A.z, 1);
+    A.w += __shfl_xor_sync(0xffffffffu, A.w, 1);
+    if (active && half == 0) {
+      const float L = sm.colL[c];
+      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+      const float4 ov = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+      const int64_t row = (int64_t)b * H * G + (int64_t)h * G + c;
+      float* orow = p.o + row * DD + 4 * d4;
+      if ((reinterpret_cast<uintptr_t>(p.o) & 15u) == 0) {
+        *reinterpret_cast<float4*>(orow) = ov;
+      } else {
+        orow[0] = ov.x; orow[1] = ov.y; orow[2] = ov.z; orow[3] = ov.w;
+      }
+      if (p.out16) {
+        uint16_t* hrow = p.out16 + row * DD + 4 * d4;
+        hrow[0] = f2h(ov.x); hrow[1] = f2h(ov.y); hrow[2] = f2h(ov.z); hrow[3] = f2h(ov.w);
+      }
+      if (d4 == 0) {
+        const float M = sm.colM[c];
+        p.lse[row] = L > 0.0f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+      }
     }
   }
   if (tid == 0) p.ctr[bh] = 0;

@@ -129,17 +129,6 @@ HX_DEVINL uint64_t radix_select(const uint64_t* cand, uint32_t cnt, uint32_t r, 
   return prefix;
 }
 
-// warp-aggregated slice counts (lanes hold consecutive pages)
-HX_DEVINL void slice_add(uint32_t* add, int sl, bool take) {
-  const uint32_t taken = __ballot_sync(0xffffffffu, take);
-  const int s0 = __shfl_sync(0xffffffffu, sl, 0), s31 = __shfl_sync(0xffffffffu, sl, 31);
-  if (s0 == s31) {
-    if (taken && (threadIdx.x & 31) == 0) atomicAdd(&add[s0], (uint32_t)__popc(taken));
-  } else if (take) {
-    atomicAdd(&add[sl], 1u);
-  }
-}
-
 // Threshold of the row (n pages, `sinks` forced, k_eff of the rest) and its
 // slices' selected counts in s.add (C slices of ceil((n - sinks) / C) pages).
 // All NT threads call it; returns T (the same in every thread).
@@ -157,6 +146,25 @@ HX_DEVINL uint64_t row_select(const float* __restrict__ sc, const uint32_t* __re
   }
   __syncthreads();
   if (trivial) return s.T;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(sc) | (uintptr_t)(sinks * 4)) & 15u) == 0;
+  // every load of the row's scores first: they are in flight while the
+  // histogram is read and its boundary found
+  constexpr int R = kFusedMaxPages / (4 * NT);
+  float vv[R][4];
+#pragma unroll
+  for (int rr = 0; rr < R; ++rr) {
+    const int j0 = sinks + rr * 4 * NT + 4 * tid;
+    if (aligned && j0 + 3 < n) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(sc + j0));
+      vv[rr][0] = f.x;
+      vv[rr][1] = f.y;
+      vv[rr][2] = f.z;
+      vv[rr][3] = f.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) vv[rr][u] = j0 + u < n ? __ldg(sc + j0 + u) : 0.0f;
+    }
+  }
   const uint32_t anchor = order_key(sc[sinks]);
   for (int i = tid; i < kBins / 4; i += NT)
     reinterpret_cast<uint4*>(s.hist)[i] = __ldcg(reinterpret_cast<const uint4*>(hist_g) + i);
@@ -174,26 +182,65 @@ HX_DEVINL uint64_t row_select(const float* __restrict__ sc, const uint32_t* __re
   __syncthreads();
   for (int i = tid; i < kBins; i += NT) s.hist[i] = 0;
   __syncthreads();
-  constexpr int U = 8;
-  for (int base = sinks; base < n; base += U * NT) {
-    float v[U];
+  // four consecutive pages a thread per round (one 16-byte load when the
+  // row is aligned): a thread's pages share a slice unless a slice starts
+  // inside them; a warp's 128 pages add to their slice with one shared add
+  // per warp and slice
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int j = base + u * NT + tid;
-      v[u] = j < n ? __ldg(sc + j) : 0.0f;
-    }
+  for (int rr = 0; rr < R; ++rr) {
+    const int base = sinks + rr * 4 * NT;
+    if (base >= n) break;
+    const int j0 = base + 4 * tid;
+    const float* v = vv[rr];
+    const int s_first = j0 < n ? (j0 - sinks) / per : -1;
+    const int s_last = j0 + 3 < n ? (j0 + 3 - sinks) / per : (j0 < n ? (n - 1 - sinks) / per : -1);
+    uint32_t cnt = 0;
+    bool mixed = s_first != s_last;
+    uint32_t cmask = 0;
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int j = base + u * NT + tid;
+    for (int u = 0; u < 4; ++u) {
+      const int j = j0 + u;
       const bool valid = j < n;
       const uint32_t k32 = order_key(v[u]);
       const int b1 = valid ? bin1(k32, anchor) : -1;
-      slice_add(s.add, valid ? (j - sinks) / per : -1, b1 > bstar || (full_bin && b1 == bstar));
-      if (b1 == bstar && !full_bin) {
-        const uint32_t at = atomicAdd(&s.nc, 1u);
-        if (at < (uint32_t)kFusedMaxPages) s.cand[at] = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)j);
-        if (split2) atomicAdd(&s.hist[bin2(k32, anchor)], 1u);
+      const bool take = b1 > bstar || (full_bin && b1 == bstar);
+      if (take) {
+        if (mixed) atomicAdd(&s.add[(j - sinks) / per], 1u);
+        else ++cnt;
       }
+      if (b1 == bstar && !full_bin) cmask |= 1u << u;
+    }
+    // slice counts: the warp's threads in one slice reduce first
+    const int w_first = __shfl_sync(0xffffffffu, s_first, 0);
+    const bool uniform = __all_sync(0xffffffffu, !mixed && (s_first == w_first || s_first < 0));
+    if (uniform) {
+      const uint32_t tot = __reduce_add_sync(0xffffffffu, cnt);
+      if ((tid & 31) == 0 && tot) atomicAdd(&s.add[w_first], tot);
+    } else if (cnt) {
+      atomicAdd(&s.add[s_first], cnt);
+    }
+    // candidates: one reservation for the warp
+    const uint32_t nmine = (uint32_t)__popc(cmask);
+    uint32_t incl = nmine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+      if ((tid & 31) >= o) incl += x;
+    }
+    const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+    if (wtot) {
+      uint32_t base0 = 0;
+      if ((tid & 31) == 31) base0 = atomicAdd(&s.nc, wtot);
+      base0 = __shfl_sync(0xffffffffu, base0, 31);
+      uint32_t at = base0 + incl - nmine;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if ((cmask >> u) & 1u) {
+          const uint32_t k32 = order_key(v[u]);
+          if (at < (uint32_t)kFusedMaxPages) s.cand[at] = ((uint64_t)k32 << 32) | (uint64_t)(~(uint32_t)(j0 + u));
+          if (split2) atomicAdd(&s.hist[bin2(k32, anchor)], 1u);
+          ++at;
+        }
     }
   }
   __syncthreads();

@@ -118,7 +118,7 @@ def lib():
 
 
 # kernel launches each entry point makes (bench.py counts launches with this)
-LAUNCHES = {"hx_scales_prepare": 2, "hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": 3, "hx_unpack_pages": 1,
+LAUNCHES = {"hx_scales_prepare": 2, "hx_pool_init": 1, "hx_pool_reset_pages": 1, "hx_pack_append": lambda a: 2 if a[7] <= 32768 else 3, "hx_unpack_pages": 1,
             "hx_nuq_pack_dense": 1, "hx_nuq_unpack_dense": 1, "hx_nuq_quantize_flat": 2,
             "hx_nuq_dequantize_flat": 1, "hx_page_stats": 1, "hx_quest_scores": 1, "hx_quest_threshold": lambda a: 1 if a[11] else 2,
             "hx_quest_threshold_slices": lambda a: 1 if a[11] else 2, "hx_quest_localize": 1,
