@@ -85,6 +85,7 @@ struct __align__(256) CtaSmem {
   alignas(256) uint16_t klut[16 * DD + 64];  // K tables (bank-spread, 256-aligned; layout at the fill)
   alignas(256) uint16_t vtail[16];           // V levels at positions >= t_cal (256-aligned)
   alignas(256) uint32_t vpair[16];           // nuq2: the same as level pairs (entry c0 | c1 << 2)
+  alignas(16) uint32_t vplane[8];            // nuq4: the same as byte planes (low bytes, then high; lut8_reg)
   int32_t pages[LISTCAP];
   int32_t phys[LISTCAP];
   uint4 dir[LISTCAP][2];                // K and V directory records of each page
@@ -137,6 +138,25 @@ HX_DEVINL uint4 lut8_nib(uint32_t w, uint32_t lowbits, uint32_t base, uint32_t o
   }
   return make_uint4(pack_u16x2(v[0], v[1]), pack_u16x2(v[2], v[3]), pack_u16x2(v[4], v[5]),
                     pack_u16x2(v[6], v[7]));
+}
+
+// 8 levels for 8 consecutive 4-bit codes of word w from a 16-entry table held
+// in registers as byte planes: lb[k] = the low bytes of levels 4k .. 4k+3, hb[k]
+// the high bytes. prmt picks a byte out of 8 by a selector nibble's low three
+// bits (bit 3, the sign-replicate flag, is cleared), so each plane half gives
+// levels code & 7 and 8 + (code & 7); a second prmt takes byte i from the first
+// or the second result by code bit 3, and a third interleaves low and high
+// bytes into fp16 pairs. No shared-memory access.
+HX_DEVINL uint4 lut8_reg(uint32_t w, const uint32_t (&lb)[4], const uint32_t (&hb)[4]) {
+  const uint32_t s = w & 0x77777777u;                  // nibble i: code_i & 7
+  const uint32_t t = ((w >> 1) & 0x44444444u) | 0x32103210u;  // nibble i: (i & 3) + 4 (code_i >> 3)
+  const uint32_t sh = s >> 16, th = t >> 16;
+  const uint32_t lo0 = prmt(prmt(lb[0], lb[1], s), prmt(lb[2], lb[3], s), t);    // low bytes, codes 0..3
+  const uint32_t hi0 = prmt(prmt(hb[0], hb[1], s), prmt(hb[2], hb[3], s), t);    // high bytes, codes 0..3
+  const uint32_t lo1 = prmt(prmt(lb[0], lb[1], sh), prmt(lb[2], lb[3], sh), th);  // codes 4..7
+  const uint32_t hi1 = prmt(prmt(hb[0], hb[1], sh), prmt(hb[2], hb[3], sh), th);
+  return make_uint4(prmt(lo0, hi0, 0x5140u), prmt(lo0, hi0, 0x7362u), prmt(lo1, hi1, 0x5140u),
+                    prmt(lo1, hi1, 0x7362u));
 }
 
 HX_DEVINL void sts128(uint32_t addr, const uint4& v) {
@@ -298,6 +318,13 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   }
   if (tid < NLV) sm.vtail[tid] = vtail_level(tid);
   if (BV == 2 && tid >= 32 && tid < 48) sm.vpair[tid - 32] = pack_u16x2(vtail_level((tid - 32) & 3), vtail_level((tid - 32) >> 2));
+  if (BV == 4 && tid >= 64 && tid < 72) {  // plane k: byte i = byte (k >> 2) of level 4 (k & 3) + i
+    const int k = tid - 64, sh = 8 * (k >> 2);
+    uint32_t v = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v |= (((uint32_t)vtail_level(4 * (k & 3) + i) >> sh) & 0xFFu) << (8 * i);
+    sm.vplane[k] = v;
+  }
   WarpSmem& ws = sm.w[warp];
   if (lane == 0 && !FSEL) {  // fused selection: after the selection, whose scratch they share
     for (int st = 0; st < NSTAGE; ++st) mbar_init(&ws.bar[st], 1);
@@ -805,10 +832,21 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
           const uint4 ca = *reinterpret_cast<const uint4*>(rowp + 16 * cx0);
           const uint4 cb = *reinterpret_cast<const uint4*>(rowp + 16 * (cx0 ^ 1));
           const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+          if (vshared) {  // one table for every token: byte planes in registers
+            const uint4 pl = *reinterpret_cast<const uint4*>(sm.vplane);
+            const uint4 ph = *reinterpret_cast<const uint4*>(sm.vplane + 4);
+            const uint32_t lb[4] = {pl.x, pl.y, pl.z, pl.w}, hb[4] = {ph.x, ph.y, ph.z, ph.w};
 #pragma unroll
-          for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < 2; ++j)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) sts128(tw4 ^ (64u * j + 16u * i), lut8_nib<0>(wv[4 * j + i], vlow, vbase, 0u));
+              for (int i = 0; i < 4; ++i) sts128(tw4 ^ (64u * j + 16u * i), lut8_reg(wv[4 * j + i], lb, hb));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                sts128(tw4 ^ (64u * j + 16u * i), lut8_nib<0>(wv[4 * j + i], vlow, vbase, 0u));
+          }
         } else {
           const uint4 c0 = *reinterpret_cast<const uint4*>(rowp);
           const uint32_t wv[4] = {c0.x, c0.y, c0.z, c0.w};
