@@ -331,7 +331,8 @@ __device__ __noinline__ ScanFix scan_fix(const uint16_t* pbase, int pstride, int
 // 31). A page with one run belongs to its warp and is written back plainly.
 // A page with several runs (tokens of the page not contiguous in the input)
 // is updated one run at a time under the record's lock, so no list entry or
-// stat is lost.
+// stat is lost; its run count, decremented as runs finish, goes from two to
+// zero, so it never reads as a one-run page.
 constexpr int PF_D = 128, PF_S = 16;
 constexpr int PF_STAGE = PF_S * PF_D;  // one run's outlier entries, staged (every element at worst)
 constexpr uint32_t kRunsOne = 1u << 8, kRunsMask = 0x7FFFFF00u, kRowsMask = 0xFFu;
@@ -628,8 +629,14 @@ __device__ __forceinline__ void pack_list_body(const hx_pool_layer& pool, const 
         rec[0] = LR.off;
         rec[1] = LR.cap;
         rec[2] = LR.cnt;
+        // A page with several runs never shows exactly one run while it is in
+        // use: a run that reads one treats the page as its own and writes its
+        // record and stats back from the copies it made without the lock, and
+        // those copies may predate another run's release. So the count goes
+        // from two straight to zero (and stays zero), and a run that reads zero
+        // or two or more takes the lock.
         const uint32_t w = __ldcg(rec + 3);
-        const uint32_t runs = (w & kRunsMask) ? (w & kRunsMask) - kRunsOne : 0u;
+        const uint32_t runs = (w & kRunsMask) > 2u * kRunsOne ? (w & kRunsMask) - kRunsOne : 0u;
         __threadfence();
         atomicExch(rec + 3, rows_new | runs);  // one run of this page done, lock clear
       }
