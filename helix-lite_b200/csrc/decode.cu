@@ -1001,6 +1001,22 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   float* wts = reinterpret_cast<float*>(sm.w);  // [n_splits][8] weights (in the warp buffers)
   float* sMv = wts + MAXSPLIT * 8;               // [n_splits][8] split maxima
   float* sLv = sMv + MAXSPLIT * 8;               // [n_splits][8] split sums
+  // two threads per (column, 4 channels): even and odd splits. A thread's
+  // first kPreSplits partial rows are loaded before anything else, so they
+  // are in flight together with the split maxima and sums below (one round
+  // trip to L2 for a merge of up to 2 kPreSplits splits)
+  constexpr int kPreSplits = 16;
+  const int item = tid >> 1, mhalf = tid & 1;
+  const bool mactive = item < G * (DD / 4);  // G * DD / 4 <= 256 groups: one pass covers them
+  const int mc = mactive ? item / (DD / 4) : 0, md4 = item % (DD / 4);
+  float4 pre[kPreSplits];
+#pragma unroll
+  for (int u = 0; u < kPreSplits; ++u) {
+    const int s = mhalf + 2 * u;
+    pre[u] = (mactive && s < p.n_splits)
+                 ? __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)s * PSZ + mc * DD) + md4)
+                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
   for (int i = tid; i < p.n_splits * 8; i += NT) {
     const int s = i >> 3, c = i & 7;
     sMv[i] = __ldcg(parts + (int64_t)s * PSZ + 8 * DD + c);
@@ -1029,16 +1045,21 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
   }
   __syncthreads();
   {
-    // two threads per (column, 4 channels): even and odd splits, eight
-    // partials in flight per pass, then one shuffle adds the halves
-    // (G * DD / 4 <= 256 groups: one pass of the block covers them all)
-    const int item = tid >> 1, half = tid & 1;
-    const bool active = item < G * (DD / 4);
-    const int c = active ? item / (DD / 4) : 0, d4 = item % (DD / 4);
+    // the preloaded partials, then any splits past them eight in flight per
+    // pass; one shuffle adds the halves
+    const int half = mhalf, c = mc, d4 = md4;
+    const bool active = mactive;
     float4 acc[2];
     acc[0] = acc[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (active) {
-      int s = half;
+#pragma unroll
+      for (int u = 0; u < kPreSplits; ++u) {
+        const int s = half + 2 * u;
+        const float w = s < p.n_splits ? wts[s * 8 + c] : 0.0f;
+        acc[u & 1].x += w * pre[u].x; acc[u & 1].y += w * pre[u].y;
+        acc[u & 1].z += w * pre[u].z; acc[u & 1].w += w * pre[u].w;
+      }
+      int s = half + 2 * kPreSplits;
       for (; s + 14 < p.n_splits; s += 16) {
         float4 v[8];
 #pragma unroll
@@ -1051,10 +1072,19 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const DecodeParams p) {
           acc[u & 1].z += w * v[u].z; acc[u & 1].w += w * v[u].w;
         }
       }
-      for (; s < p.n_splits; s += 2) {
-        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)s * PSZ + c * DD) + d4);
-        const float w0 = wts[s * 8 + c];
-        acc[0].x += w0 * v0.x; acc[0].y += w0 * v0.y; acc[0].z += w0 * v0.z; acc[0].w += w0 * v0.w;
+      for (; s < p.n_splits; s += 8) {  // the last up to four, loaded together
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          v[u] = s + 2 * u < p.n_splits
+                     ? __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)(s + 2 * u) * PSZ + c * DD) + d4)
+                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float w = s + 2 * u < p.n_splits ? wts[(s + 2 * u) * 8 + c] : 0.0f;
+          acc[u & 1].x += w * v[u].x; acc[u & 1].y += w * v[u].y;
+          acc[u & 1].z += w * v[u].z; acc[u & 1].w += w * v[u].w;
+        }
       }
     }
     float4 A = make_float4(acc[0].x + acc[1].x, acc[0].y + acc[1].y, acc[0].z + acc[1].z, acc[0].w + acc[1].w);

@@ -263,9 +263,7 @@ struct __align__(128) QuestSmem {
 // by the same arithmetic as the batched scoring; lane l holds channels
 // 4l .. 4l+3 of the group terms.
 HX_DEVINL uint32_t anchor_key_d128(const uint16_t* __restrict__ kmin, int64_t page_stride, int64_t head_stride,
-                                   const int32_t* __restrict__ bt, int bt_stride, int b, int h, int a,
-                                   const float* qp, const float* qn, int lane) {
-  const int64_t phys = bt ? (int64_t)bt[(int64_t)b * bt_stride + a] : (int64_t)a;
+                                   int64_t phys, int h, const float* qp, const float* qn, int lane) {
   const uint16_t* pm = kmin + phys * page_stride + (int64_t)h * head_stride;
   const uint2 c = *reinterpret_cast<const uint2*>(pm + 4 * lane);
   const uint2 x = *reinterpret_cast<const uint2*>(pm + 128 + 4 * lane);
@@ -289,9 +287,7 @@ HX_DEVINL uint32_t anchor_key_d128(const uint16_t* __restrict__ kmin, int64_t pa
 HX_DEVINL void group_terms4(const uint16_t* __restrict__ q, int64_t qbase, int G, int mode, int lane, float* qp,
                             float* qn) {
   float s[4] = {0.0f, 0.0f, 0.0f, 0.0f}, t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 4
-  for (int g = 0; g < G; ++g) {
-    const uint2 w = *reinterpret_cast<const uint2*>(q + qbase + (int64_t)g * 128 + 4 * lane);
+  auto add = [&](uint2 w) {
     const float x[4] = {h2f((uint16_t)(w.x & 0xffff)), h2f((uint16_t)(w.x >> 16)), h2f((uint16_t)(w.y & 0xffff)),
                         h2f((uint16_t)(w.y >> 16))};
 #pragma unroll
@@ -303,7 +299,18 @@ HX_DEVINL void group_terms4(const uint16_t* __restrict__ q, int64_t qbase, int G
         s[v] = __fadd_rn(s[v], x[v]);
       }
     }
-  }
+  };
+  // the first kPre heads' rows are all loaded before the sums (one round trip),
+  // then added in head order like any further ones
+  constexpr int kPre = 8;
+  uint2 wv[kPre];
+#pragma unroll
+  for (int g = 0; g < kPre; ++g)
+    wv[g] = g < G ? *reinterpret_cast<const uint2*>(q + qbase + (int64_t)g * 128 + 4 * lane) : make_uint2(0u, 0u);
+#pragma unroll
+  for (int g = 0; g < kPre; ++g)
+    if (g < G) add(wv[g]);
+  for (int g = kPre; g < G; ++g) add(*reinterpret_cast<const uint2*>(q + qbase + (int64_t)g * 128 + 4 * lane));
 #pragma unroll
   for (int v = 0; v < 4; ++v) {
     if (mode == 0) {
@@ -342,7 +349,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   // batch k of this warp is global batch g0 + k. For a batch: its pages count
   // (lanes < cnt hold a page), the sequence's sinks, lane's physical page.
   struct Bat {
-    int bh, j0, cnt, sinks;
+    int bh, j0, cnt, sinks, n;
     int64_t phys;
   };
   // The planner walks the warp's batches in order, so (b, h) and the batch
@@ -364,6 +371,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     if (first || pl_jb == 0) pl_n = min((seq_lens[b] + S - 1) / S, max_pages);
     r.cnt = max(0, min(kQPB, pl_n - r.j0));
     r.sinks = min(max(sinks_req, 0), pl_n);
+    r.n = pl_n;
     const int j = r.j0 + lane;
     r.phys = (lane < r.cnt) ? (bt ? (int64_t)bt[(int64_t)b * bt_stride + j] : (int64_t)j) : 0;
     return r;
@@ -395,7 +403,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   // the block's batches are contiguous: its first rows are counted in smem
   const int bh0 = (int)min((int64_t)blockIdx.x * kQW * per, total) / nb;
   const int nk = (int)max((int64_t)0, min(per, total - g0));
-  Bat p0 = {0, 0, 0, 0, 0}, p1 = {0, 0, 0, 0, 0}, p2 = {0, 0, 0, 0, 0};
+  Bat p0 = {0, 0, 0, 0, 0, 0}, p1 = {0, 0, 0, 0, 0, 0}, p2 = {0, 0, 0, 0, 0, 0};
   if (nk > 0) p0 = plan_next(true, g0);
   if (nk > 1) p1 = plan_next(false, 0);
   if (nk > 2) p2 = plan_next(false, 0);
@@ -410,19 +418,19 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     // keep two batches in flight: issue k + 2 now, plan k + 3 (its block-table
     // reads overlap this batch's work)
     if (k + 2 < nk) issue(p2, (k + 2) % kQStages);
-    Bat p3 = {0, 0, 0, 0, 0};
+    Bat p3 = {0, 0, 0, 0, 0, 0};
     if (k + 3 < nk) p3 = plan_next(false, 0);
     const Bat cb = p0;
     if (cb.cnt > 0) {
       if (cb.bh != cur_bh) {
         const int b = cb.bh / H, h = cb.bh % H;
+        // the row's anchor (page `sinks`, when there is one): its block-table
+        // entry is loaded together with the query rows, its stats after
+        const bool has_anchor = hist && cb.sinks < cb.n;
+        const int64_t aphys =
+            has_anchor ? (bt ? (int64_t)bt[(int64_t)b * bt_stride + cb.sinks] : (int64_t)cb.sinks) : 0;
         group_terms4(q, ((int64_t)b * H * G + (int64_t)h * G) * 128, G, mode, lane, qp, qn);
-        if (hist) {  // the row's anchor: page `sinks`, when there is one
-          const int n = min((seq_lens[b] + S - 1) / S, max_pages);
-          anchor = cb.sinks < n
-                       ? anchor_key_d128(kmin, page_stride, head_stride, bt, bt_stride, b, h, cb.sinks, qp, qn, lane)
-                       : 0u;
-        }
+        anchor = has_anchor ? anchor_key_d128(kmin, page_stride, head_stride, aphys, h, qp, qn, lane) : 0u;
         cur_bh = cb.bh;
       }
       if (!dead && !mbar_wait(&sm.bar[warp][st], (phase >> st) & 1u)) {
