@@ -138,6 +138,13 @@ HX_DEVINL uint64_t row_select(const float* __restrict__ sc, const uint32_t* __re
   const int tid = threadIdx.x;
   const int n_ns = n - sinks;
   const int per = n_ns > 0 ? (n_ns + C - 1) / C : 1;
+  // slice of a non-sink offset x (0 <= x < kFusedMaxPages): x / per by a
+  // multiply with per's rounded-up 32-bit reciprocal, exact for every x below
+  // 2^18 and per >= 2 (checked for all x, per < 2^14 + 1); per = 1 is x itself.
+  // The division it replaces cost two ~35-instruction sequences a thread and
+  // round, 0.74 of the pass's 1.2 us a round at 8,192 pages on B200.
+  const uint32_t per_m = per > 1 ? (uint32_t)((0x100000000ull + (uint64_t)per - 1ull) / (uint64_t)per) : 0u;
+  auto slice_of = [&](int x) -> int { return per > 1 ? (int)__umulhi((uint32_t)x, per_m) : x; };
   const bool trivial = k_eff == 0 || k_eff >= n_ns;
   for (int i = tid; i < C; i += NT) s.add[i] = (trivial && k_eff > 0) ? (uint32_t)max(0, min(per, n_ns - i * per)) : 0u;
   if (tid == 0) {
@@ -192,8 +199,8 @@ HX_DEVINL uint64_t row_select(const float* __restrict__ sc, const uint32_t* __re
     if (base >= n) break;
     const int j0 = base + 4 * tid;
     const float* v = vv[rr];
-    const int s_first = j0 < n ? (j0 - sinks) / per : -1;
-    const int s_last = j0 + 3 < n ? (j0 + 3 - sinks) / per : (j0 < n ? (n - 1 - sinks) / per : -1);
+    const int s_first = j0 < n ? slice_of(j0 - sinks) : -1;
+    const int s_last = j0 + 3 < n ? slice_of(j0 + 3 - sinks) : (j0 < n ? slice_of(n - 1 - sinks) : -1);
     uint32_t cnt = 0;
     bool mixed = s_first != s_last;
     uint32_t cmask = 0;
@@ -205,7 +212,7 @@ HX_DEVINL uint64_t row_select(const float* __restrict__ sc, const uint32_t* __re
       const int b1 = valid ? bin1(k32, anchor) : -1;
       const bool take = b1 > bstar || (full_bin && b1 == bstar);
       if (take) {
-        if (mixed) atomicAdd(&s.add[(j - sinks) / per], 1u);
+        if (mixed) atomicAdd(&s.add[slice_of(j - sinks)], 1u);
         else ++cnt;
       }
       if (b1 == bstar && !full_bin) cmask |= 1u << u;
@@ -300,7 +307,7 @@ HX_DEVINL uint64_t row_select(const float* __restrict__ sc, const uint32_t* __re
   if (!full_bin)
     for (uint32_t i = tid; i < cnt; i += NT) {
       const uint64_t key = s.cand[i];
-      if (key >= T) atomicAdd(&s.add[min(((int)(~(uint32_t)key) - sinks) / per, C - 1)], 1u);
+      if (key >= T) atomicAdd(&s.add[min(slice_of((int)(~(uint32_t)key) - sinks), C - 1)], 1u);
     }
   if (tid == 0) s.T = T;
   __syncthreads();
