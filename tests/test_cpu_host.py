@@ -193,3 +193,15 @@ def test_global_selection_score_gather_two_gloo_ranks(tmp_path):
     want = np.concatenate([base, base + 1000], axis=2)
     for r in range(2):
         np.testing.assert_array_equal(np.load(tmp_path / f"g{r}.npy"), want)
+
+
+def test_slice_index_by_reciprocal_multiply_is_exact():
+    """The fused selection (csrc/select.cuh, row_select) finds a page's slice
+    as (x * m) >> 32 with m = ceil(2^32 / per) instead of x / per. That is the
+    quotient for every non-sink offset x the kernel can meet (x < 16,384, the
+    fused-selection row limit) and every slice width 2 <= per <= 16,384; width
+    1 takes x itself. Checked exhaustively here."""
+    x = np.arange(16384, dtype=np.uint64)
+    for per in range(2, 16385):
+        m = np.uint64(((1 << 32) + per - 1) // per)
+        assert np.array_equal((x * m) >> np.uint64(32), x // np.uint64(per)), per
