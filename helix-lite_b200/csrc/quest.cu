@@ -349,25 +349,33 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   // batch k of this warp is global batch g0 + k. For a batch: its pages count
   // (lanes < cnt hold a page), the sequence's sinks, lane's physical page.
   struct Bat {
-    int bh, j0, cnt, sinks, n;
+    int bh, b, h, j0, cnt, sinks, n;
     int64_t phys;
   };
   // The planner walks the warp's batches in order, so (b, h) and the batch
   // index advance by counting, and a sequence's length is read once per (b, h):
   // no division and no dependent global load per batch.
-  int pl_bh = -1, pl_jb = 0, pl_n = 0;
+  int pl_bh = -1, pl_b = 0, pl_h = 0, pl_jb = 0, pl_n = 0;
   auto plan_next = [&](bool first, int64_t it) -> Bat {
     if (first) {
       pl_bh = (int)(it / nb);
       pl_jb = (int)(it % nb);
+      pl_b = pl_bh / H;
+      pl_h = pl_bh % H;
     } else if (++pl_jb == nb) {
       pl_jb = 0;
       ++pl_bh;
+      if (++pl_h == H) {
+        pl_h = 0;
+        ++pl_b;
+      }
     }
     Bat r;
     r.bh = pl_bh;
+    r.b = pl_b;
+    r.h = pl_h;
     r.j0 = pl_jb * kQPB;
-    const int b = r.bh / H;
+    const int b = pl_b;
     if (first || pl_jb == 0) pl_n = min((seq_lens[b] + S - 1) / S, max_pages);
     r.cnt = max(0, min(kQPB, pl_n - r.j0));
     r.sinks = min(max(sinks_req, 0), pl_n);
@@ -393,7 +401,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     if (start) {
       const uint32_t later = starts & ~((2u << lane) - 1u);  // run starts after this lane
       const int end = later ? __ffs(later) - 1 : bb.cnt;
-      bulk_g2s(sm.rec[warp][st][lane], kmin + bb.phys * page_stride + (int64_t)(bb.bh % H) * head_stride,
+      bulk_g2s(sm.rec[warp][st][lane], kmin + bb.phys * page_stride + (int64_t)bb.h * head_stride,
                512u * (uint32_t)(end - lane), &sm.bar[warp][st]);
     }
   };
@@ -403,7 +411,7 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
   // the block's batches are contiguous: its first rows are counted in smem
   const int bh0 = (int)min((int64_t)blockIdx.x * kQW * per, total) / nb;
   const int nk = (int)max((int64_t)0, min(per, total - g0));
-  Bat p0 = {0, 0, 0, 0, 0, 0}, p1 = {0, 0, 0, 0, 0, 0}, p2 = {0, 0, 0, 0, 0, 0};
+  Bat p0 = {0, 0, 0, 0, 0, 0, 0, 0}, p1 = {0, 0, 0, 0, 0, 0, 0, 0}, p2 = {0, 0, 0, 0, 0, 0, 0, 0};
   if (nk > 0) p0 = plan_next(true, g0);
   if (nk > 1) p1 = plan_next(false, 0);
   if (nk > 2) p2 = plan_next(false, 0);
@@ -418,12 +426,12 @@ __global__ void __launch_bounds__(kQW * 32) quest_scores_tma_kernel(
     // keep two batches in flight: issue k + 2 now, plan k + 3 (its block-table
     // reads overlap this batch's work)
     if (k + 2 < nk) issue(p2, (k + 2) % kQStages);
-    Bat p3 = {0, 0, 0, 0, 0, 0};
+    Bat p3 = {0, 0, 0, 0, 0, 0, 0, 0};
     if (k + 3 < nk) p3 = plan_next(false, 0);
     const Bat cb = p0;
     if (cb.cnt > 0) {
       if (cb.bh != cur_bh) {
-        const int b = cb.bh / H, h = cb.bh % H;
+        const int b = cb.b, h = cb.h;
         // the row's anchor (page `sinks`, when there is one): its block-table
         // entry is loaded together with the query rows, its stats after
         const bool has_anchor = hist && cb.sinks < cb.n;
